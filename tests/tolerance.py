@@ -1,0 +1,51 @@
+"""Matmul parity tolerance shared by the CPU oracle tests and the GPU tests.
+
+The north-star bar is: max-abs error <= 1e-2 x RMS(reference output), for bf16
+inputs with fp32 accumulation.  Outputs are stored in the activation dtype, so
+two correct implementations that sum in different orders can land one output
+ulp apart wherever the fp32 sum sits next to a rounding boundary; for bf16 one
+ulp exceeds 1e-2 x RMS as soon as |y| >= 2 x RMS.  The check is therefore
+
+    |y - y_ref| <= 1e-2 * rms(y_ref) + ulp(y_ref)     (elementwise)
+
+where ulp is one unit in the last place of the stored dtype at y_ref (0 for
+fp32).  ``matmul_error`` also reports the plain max-abs / RMS figure.
+"""
+import numpy as np
+
+RTOL_RMS = 1e-2
+F32, BF16, F16 = 0, 1, 2
+_MANT = {BF16: 7, F16: 10}
+
+
+def ulp(y, dtype):
+    if dtype not in _MANT:
+        return np.zeros_like(y, dtype=np.float64)
+    a = np.abs(y.astype(np.float64))
+    e = np.floor(np.log2(np.where(a > 0, a, 1.0)))
+    if dtype == F16:
+        e = np.maximum(e, -14)
+    return np.where(a > 0, np.exp2(e - _MANT[dtype]), 0.0)
+
+
+def matmul_error(y, y_ref):
+    y = np.asarray(y, np.float64)
+    y_ref = np.asarray(y_ref, np.float64)
+    rms = float(np.sqrt(np.mean(y_ref ** 2))) if y_ref.size else 0.0
+    err = float(np.max(np.abs(y - y_ref))) if y_ref.size else 0.0
+    return err, rms
+
+
+def assert_matmul_close(y, y_ref, dtype):
+    y = np.asarray(y, np.float64)
+    y_ref = np.asarray(y_ref, np.float64)
+    assert y.shape == y_ref.shape, (y.shape, y_ref.shape)
+    assert np.all(np.isfinite(y)), "non-finite output"
+    err, rms = matmul_error(y, y_ref)
+    bound = RTOL_RMS * rms + ulp(y_ref, dtype)
+    bad = np.abs(y - y_ref) > bound
+    if bad.any():
+        i = np.argmax(np.abs(y - y_ref) - bound)
+        raise AssertionError(
+            f"{int(bad.sum())}/{y.size} outputs outside 1e-2*RMS + 1 ulp: max-abs {err:.4g}, "
+            f"rms {rms:.4g}; worst at flat {i}: {y.reshape(-1)[i]!r} vs {y_ref.reshape(-1)[i]!r}")
