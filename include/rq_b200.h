@@ -1,0 +1,170 @@
+/*
+ * rq_b200.h -- C ABI of the B200 (sm_100a) implementation of rocm-qlora's
+ * quantize / dequantize / QuantLinear+LoRA hot path.
+ *
+ * Conventions (every rq_* entry point):
+ *   - plain device pointers and sizes; no framework types;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default);
+ *   - nothing is allocated: callers own inputs, outputs and workspace;
+ *   - the return value is RQ_OK (0) or a negative RQ_ERR_* status; the
+ *     arguments are validated on the host before any launch, and a launch
+ *     failure is reported as RQ_ERR_CUDA (rq_last_cuda_error() has the code);
+ *   - calls are asynchronous on `stream` and thread-safe for distinct
+ *     streams; a workspace must not be shared by calls that may overlap.
+ *
+ * Dtype codes: RQ_F32, RQ_BF16, RQ_F16.  Weight formats: RQ_W_* below.
+ * Layouts follow the reference exactly (rocm_qlora/quantization):
+ *   NF4 codes: flat row-major [N*K] elements, padded with zeros to a multiple
+ *     of block_size, two codes per byte, byte i = code[2i] | code[2i+1] << 4;
+ *   NF4 scales: one absmax per block, in the weight's dtype;
+ *   double quant: c2 = one fp8-e4m3fnuz (or int8) byte per block, padded to a
+ *     multiple of 256; c2_scales = fp32 absmax per 256 blocks;
+ *   INT8 blockwise: int8 [N*K padded], scales per block (weight dtype);
+ *   INT8 per-row: int8 [N, K], scales [N] (weight dtype).
+ */
+#ifndef RQ_B200_H
+#define RQ_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RQ_API __attribute__((visibility("default")))
+#else
+#define RQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RQ_OK 0
+#define RQ_ERR_INVALID (-1)     /* bad size, null pointer, bad parameter */
+#define RQ_ERR_ALIGN (-2)       /* pointer not aligned as required */
+#define RQ_ERR_DTYPE (-3)       /* unsupported dtype / format code */
+#define RQ_ERR_CUDA (-4)        /* CUDA launch or runtime error */
+#define RQ_ERR_WORKSPACE (-5)   /* workspace missing or too small */
+#define RQ_ERR_DEVICE (-6)      /* current device is not sm_100 */
+
+#define RQ_F32 0
+#define RQ_BF16 1
+#define RQ_F16 2
+
+#define RQ_W_NF4 0          /* NF4 codes + per-block scales */
+#define RQ_W_NF4_DQ_FP8 1   /* NF4 codes + fp8-e4m3fnuz c2 + fp32 c2_scales */
+#define RQ_W_NF4_DQ_INT8 2  /* NF4 codes + int8 c2 + fp32 c2_scales */
+#define RQ_W_INT8 3         /* int8 blockwise */
+#define RQ_W_INT8_ROW 4     /* int8 per output row (per_channel=True) */
+
+/* ------------------------------------------------------------ utilities */
+RQ_API int rq_abi_version(void);                 /* bumps on any ABI change */
+RQ_API const char* rq_status_string(int status);
+RQ_API int rq_last_cuda_error(void);             /* cudaError_t of the last RQ_ERR_CUDA in this thread */
+
+/* -------------------------------------------------------- quantization */
+
+/* NF4 blockwise quantization of x[numel] (dtype RQ_F32/BF16/F16).
+ * packed: ceil(numel/bs)*bs/2 bytes; scales: ceil(numel/bs) values of dtype.
+ * block_size must be even and >= 2.
+ * Replaces quantize_int4, rocm_qlora/quantization/quant_ops.py:80-126. */
+RQ_API int rq_nf4_quantize(const void* x, int dtype, int64_t numel, int block_size,
+                    uint8_t* packed, void* scales, void* stream);
+
+/* NF4 dequantization of `nbytes` packed bytes (2*nbytes values) with
+ * per-block scales of scale_dtype into out (out_dtype; RQ_F32 gives the
+ * reference's fp32 result, RQ_BF16/RQ_F16 that value rounded).
+ * Replaces dequantize_int4, quant_ops.py:128-150, and
+ * dequantize_nf4_triton, rocm_qlora/kernels/nf4_dequant.py:81-115. */
+RQ_API int rq_nf4_dequantize(const uint8_t* packed, int64_t nbytes, const void* scales,
+                      int scale_dtype, int block_size, void* out, int out_dtype,
+                      void* stream);
+
+/* INT8 blockwise quantization: q[ceil(numel/bs)*bs], scales[ceil(numel/bs)].
+ * Replaces quantize_int8(per_channel=False), quant_ops.py:36-53. */
+RQ_API int rq_int8_quantize(const void* x, int dtype, int64_t numel, int block_size,
+                     int8_t* q, void* scales, void* stream);
+
+/* INT8 per-row quantization of x[rows, cols]: q[rows, cols], scales[rows].
+ * Replaces quantize_int8(per_channel=True), quant_ops.py:28-35. */
+RQ_API int rq_int8_quantize_rows(const void* x, int dtype, int64_t rows, int64_t cols,
+                          int8_t* q, void* scales, void* stream);
+
+/* INT8 dequantization of q[numel]; cols > 0 selects per-row scales (row =
+ * i / cols), else blockwise with block_size.
+ * Replaces dequantize_int8, quant_ops.py:55-78. */
+RQ_API int rq_int8_dequantize(const int8_t* q, int64_t numel, const void* scales,
+                       int scale_dtype, int block_size, int64_t cols, void* out,
+                       int out_dtype, void* stream);
+
+/* Second-level quantization of nb fp32 first-level scales c1:
+ * c2[ceil(nb/block2)*block2] (fp8 e4m3fnuz bytes if fp8 != 0, else int8),
+ * c2_scales[ceil(nb/block2)] fp32.
+ * Replaces double_quantize lines 58-97, rocm_qlora/quantization/double_quant.py. */
+RQ_API int rq_dq_quantize_scales(const float* c1, int64_t nb, int block2, int fp8,
+                          uint8_t* c2, float* c2_scales, void* stream);
+
+/* Double-quantized NF4 dequantization of `numel` values:
+ * out[i] = T[code_i] * (c2[i/bs] * c2_scales[i/bs/block2]).
+ * Replaces double_dequantize, double_quant.py:99-122. */
+RQ_API int rq_dq_dequantize(const uint8_t* packed, int64_t numel, const uint8_t* c2,
+                     const float* c2_scales, int fp8, int block_size, int block2,
+                     void* out, int out_dtype, void* stream);
+
+/* ------------------------------------------------ QuantLinear + LoRA */
+
+/* Bytes of workspace rq_linear_forward / rq_linear_dx need for these sizes
+ * (0 is possible).  The first 256 bytes of a workspace are a counter area
+ * that must be zero before its first use; the kernels leave it zero. */
+RQ_API int64_t rq_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int r);
+
+/* y[M,N] = base + lora where, in the activation dtype `xdtype`,
+ *   base = round(x[M,K] . deq(W)^T + bias)          (fp32 accumulation)
+ *   lora = round(round(round(x . A^T) . B^T) * scaling)
+ *   y    = round(base + lora)
+ * i.e. LoRALinear.forward in eval mode over QuantLinear.forward
+ * (rocm_qlora/lora/lora_layer.py:51-70, quantization/quant_linear.py:121-197,
+ * kernels/dequant_matmul.py:356-376).  W is [N, K] in format `wfmt`:
+ *   qweight  NF4 packed codes / int8 values (layout above);
+ *   scales   per-block (or per-row) scales of scale_dtype (unused for DQ);
+ *   c2, c2_scales  double-quant second level (DQ formats only).
+ * bias [N] (bias_dtype) may be NULL; lora_a [r,K] and lora_b [N,r] are in
+ * xdtype and may both be NULL (r = 0).  lora_x [M,K] is the input of the
+ * adapter branch when it differs from x (LoRA dropout in training,
+ * lora_layer.py:67); NULL means x.  x, y contiguous row-major.
+ * xdtype: RQ_BF16 or RQ_F16 (tensor-core paths) or RQ_F32. */
+RQ_API int rq_linear_forward(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                      const uint8_t* c2, const float* c2_scales,
+                      int64_t N, int64_t K, int block_size,
+                      const void* x, int xdtype, int64_t M, const void* lora_x,
+                      const void* bias, int bias_dtype,
+                      const void* lora_a, const void* lora_b, int r, float scaling,
+                      void* y, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* dx[M,K] = round(round(dy . deq(W)) + round(round(round(dy*scaling) . B) . A)),
+ * the input gradient of the same layer (autograd of lora_layer.py:67 with a
+ * frozen base; kernels/dequant_matmul.py:337-351 for the base term). */
+RQ_API int rq_linear_dx(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                 const uint8_t* c2, const float* c2_scales,
+                 int64_t N, int64_t K, int block_size,
+                 const void* dy, int xdtype, int64_t M,
+                 const void* lora_a, const void* lora_b, int r, float scaling,
+                 void* dx, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------- reference launcher drop-ins */
+
+/* Same symbol names, argument order and types as the reference's HIP
+ * launchers (rocm_qlora/hip_kernels/int4_matmul.hip:413-458, bound by
+ * ctypes in rocm_qlora/hip_kernels/build_utils.py:237-262): x fp16 [M,K],
+ * scales fp16 per 64-block as declared there, c fp16 [M,N], no bias.  They
+ * return void like the originals; the status of the last call is available
+ * from rq_last_status(). */
+RQ_API void launch_int4_dequant_matmul(void* stream, void* x, void* w_packed, void* scales,
+                                void* c, int M, int N, int K, int block_size);
+RQ_API void launch_int8_dequant_matmul(void* stream, void* x, void* w_int8, void* scales,
+                                void* c, int M, int N, int K, int block_size);
+RQ_API int rq_last_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RQ_B200_H */

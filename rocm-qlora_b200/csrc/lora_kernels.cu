@@ -1,0 +1,237 @@
+// lora_kernels.cu -- the rank-r "down" products of the LoRA adapter.
+//
+//   forward: t[M, r]  = rnd(x[M, K] . A[r, K]^T)            (lora_layer.py:67, x @ A.T)
+//   dx:      gt[M, r] = rnd(rnd(dy[M, N] * s) . B[N, r])     (autograd of (.. @ B.T) * s)
+//
+// Both are skinny GEMMs (r <= 128).  They run on the tensor cores with
+// mma.sync m16n8k16 (fp32 accumulation); when M is small the reduction
+// dimension is split across CTAs and the fp32 partials are summed in a
+// fixed order by the last CTA to finish (arrival counter in the workspace
+// counter area, reset by that CTA), so results are deterministic.
+#include <cuda_runtime.h>
+
+#include "linear_common.cuh"
+
+namespace rq {
+
+template <int DT> struct MmaOp;
+template <> struct MmaOp<RQ_BF16> {
+  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+template <> struct MmaOp<RQ_F16> {
+  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+
+template <int DT>
+__device__ __forceinline__ uint16_t bits16(typename DType<DT>::T v) {
+  return *reinterpret_cast<uint16_t*>(&v);
+}
+
+// Two consecutive 16-bit elements p[i], p[i+1] (zero past `lim`).
+template <int DT>
+__device__ __forceinline__ uint32_t ld_pair(const typename DType<DT>::T* p, int64_t i, int64_t lim, bool vec_ok) {
+  if (vec_ok && i + 1 < lim) return *reinterpret_cast<const uint32_t*>(p + i);
+  const uint32_t lo = i < lim ? bits16<DT>(p[i]) : 0u;
+  const uint32_t hi = i + 1 < lim ? bits16<DT>(p[i + 1]) : 0u;
+  return lo | (hi << 16);
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t prescale_pair(uint32_t v, float s) {
+  using T = typename DType<DT>::T;
+  const uint16_t lo = (uint16_t)(v & 0xFFFFu), hi = (uint16_t)(v >> 16);
+  const float a = DType<DT>::to_f32(*reinterpret_cast<const T*>(&lo)) * s;
+  const float b = DType<DT>::to_f32(*reinterpret_cast<const T*>(&hi)) * s;
+  return pack2<DT>(a, b);
+}
+
+constexpr int kLoraMaxR = 128;
+
+// out[M, R] = rnd(pre(X)[M, Kr] . W2^T);  W2 is [R, Kr] (WT = false) or
+// [Kr, R] (WT = true).  grid = (ceil(M / (16*WM)), ksplit).
+template <int DT, bool WT, int WM>
+__global__ void __launch_bounds__(32 * WM) lora_down_mma_k(const typename DType<DT>::T* __restrict__ X, int64_t M,
+                                                           int64_t Kr, const typename DType<DT>::T* __restrict__ W2,
+                                                           int R, float pre_s, int do_pre, int kchunk,
+                                                           float* __restrict__ partial, unsigned* __restrict__ counters,
+                                                           typename DType<DT>::T* __restrict__ out) {
+  using T = typename DType<DT>::T;
+  constexpr int NT = kLoraMaxR / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t m0 = ((int64_t)blockIdx.x * WM + warp) * 16;
+  const int64_t kbeg = (int64_t)blockIdx.y * kchunk;
+  const int64_t kend = kbeg + kchunk < Kr ? kbeg + kchunk : Kr;
+  const int ntiles = (R + 7) / 8;
+  const bool vec_x = ((uintptr_t)X % 4 == 0) && (Kr % 2 == 0);
+  const bool vec_w = ((uintptr_t)W2 % 4 == 0) && (Kr % 2 == 0);
+  float acc[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+
+  const int64_t ra = m0 + g, rb = m0 + g + 8;
+  const T* xa = X + (ra < M ? ra : 0) * Kr;
+  const T* xb = X + (rb < M ? rb : 0) * Kr;
+  for (int64_t k0 = kbeg; k0 < kend; k0 += 16) {
+    uint32_t a[4];
+    a[0] = ra < M ? ld_pair<DT>(xa, k0 + 2 * t, kend, vec_x) : 0u;
+    a[1] = rb < M ? ld_pair<DT>(xb, k0 + 2 * t, kend, vec_x) : 0u;
+    a[2] = ra < M ? ld_pair<DT>(xa, k0 + 8 + 2 * t, kend, vec_x) : 0u;
+    a[3] = rb < M ? ld_pair<DT>(xb, k0 + 8 + 2 * t, kend, vec_x) : 0u;
+    if (do_pre) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = prescale_pair<DT>(a[i], pre_s);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (nt < ntiles) {
+        const int n = nt * 8 + g;
+        uint32_t b0 = 0, b1 = 0;
+        if (n < R) {
+          if (!WT) {
+            b0 = ld_pair<DT>(W2 + (int64_t)n * Kr, k0 + 2 * t, kend, vec_w);
+            b1 = ld_pair<DT>(W2 + (int64_t)n * Kr, k0 + 8 + 2 * t, kend, vec_w);
+          } else {
+            const int64_t ka = k0 + 2 * t, kb = k0 + 8 + 2 * t;
+            const uint32_t e0 = ka < kend ? bits16<DT>(W2[ka * R + n]) : 0u;
+            const uint32_t e1 = ka + 1 < kend ? bits16<DT>(W2[(ka + 1) * R + n]) : 0u;
+            const uint32_t e2 = kb < kend ? bits16<DT>(W2[kb * R + n]) : 0u;
+            const uint32_t e3 = kb + 1 < kend ? bits16<DT>(W2[(kb + 1) * R + n]) : 0u;
+            b0 = e0 | (e1 << 16);
+            b1 = e2 | (e3 << 16);
+          }
+        }
+        MmaOp<DT>::mma(acc[nt], a, b0, b1);
+      }
+    }
+  }
+
+  if (gridDim.y == 1) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (nt < ntiles) {
+        const int c = nt * 8 + 2 * t;
+        if (ra < M && c < R) out[ra * R + c] = DType<DT>::from_f32(acc[nt][0]);
+        if (ra < M && c + 1 < R) out[ra * R + c + 1] = DType<DT>::from_f32(acc[nt][1]);
+        if (rb < M && c < R) out[rb * R + c] = DType<DT>::from_f32(acc[nt][2]);
+        if (rb < M && c + 1 < R) out[rb * R + c + 1] = DType<DT>::from_f32(acc[nt][3]);
+      }
+    }
+    return;
+  }
+  // split-K: partial[split][m][c] fp32, the last CTA of this M-tile sums
+  float* mypart = partial + (int64_t)blockIdx.y * M * R;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    if (nt < ntiles) {
+      const int c = nt * 8 + 2 * t;
+      if (ra < M && c < R) mypart[ra * R + c] = acc[nt][0];
+      if (ra < M && c + 1 < R) mypart[ra * R + c + 1] = acc[nt][1];
+      if (rb < M && c < R) mypart[rb * R + c] = acc[nt][2];
+      if (rb < M && c + 1 < R) mypart[rb * R + c + 1] = acc[nt][3];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ unsigned ticket;
+  if (threadIdx.x == 0) ticket = atomicAdd(&counters[blockIdx.x], 1u);
+  __syncthreads();
+  if (ticket != gridDim.y - 1) return;
+  __threadfence();
+  const int64_t mt0 = (int64_t)blockIdx.x * WM * 16;
+  const int64_t mt1 = mt0 + WM * 16 < M ? mt0 + WM * 16 : M;
+  for (int64_t i = threadIdx.x; i < (mt1 - mt0) * R; i += blockDim.x) {
+    const int64_t m = mt0 + i / R, c = i % R;
+    float s = 0.0f;
+    for (unsigned sp = 0; sp < gridDim.y; ++sp) s += __ldcg(&partial[(int64_t)sp * M * R + m * R + c]);
+    out[m * R + c] = DType<DT>::from_f32(s);
+  }
+  if (threadIdx.x == 0) counters[blockIdx.x] = 0u;  // leave the counter area zeroed
+}
+
+// fp32 activations: one thread per output, CUDA cores.
+template <bool WT>
+__global__ void __launch_bounds__(256) lora_down_f32_k(const float* __restrict__ X, int64_t M, int64_t Kr,
+                                                       const float* __restrict__ W2, int R, float pre_s, int do_pre,
+                                                       float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * R) return;
+  const int64_t m = i / R, c = i % R;
+  float acc = 0.0f;
+  for (int64_t k = 0; k < Kr; ++k) {
+    float xv = X[m * Kr + k];
+    if (do_pre) xv = xv * pre_s;
+    const float wv = WT ? W2[k * R + c] : W2[c * Kr + k];
+    acc = fmaf(xv, wv, acc);
+  }
+  out[i] = acc;
+}
+
+template <int DT, bool WT>
+static int lora_down_t(const void* X, int64_t M, int64_t Kr, const void* W2, int R, float pre_s, int do_pre,
+                       void* out, float* partial, int64_t partial_elems, unsigned* counters, int ncounters,
+                       cudaStream_t st) {
+  using T = typename DType<DT>::T;
+  if (M <= 16) {
+    // split the reduction so that ~128 single-warp CTAs share it
+    int64_t ksplit = Kr / 256;
+    if (ksplit > 128) ksplit = 128;
+    if (ksplit > partial_elems / (M * R)) ksplit = partial_elems / (M * R);
+    if (ksplit < 1) ksplit = 1;
+    int64_t kchunk = (Kr + ksplit - 1) / ksplit;
+    kchunk = (kchunk + 15) / 16 * 16;
+    ksplit = (Kr + kchunk - 1) / kchunk;
+    if (ksplit > 1 && ncounters < 1) ksplit = 1, kchunk = Kr;
+    lora_down_mma_k<DT, WT, 1><<<dim3(1, (unsigned)ksplit), 32, 0, st>>>(
+        (const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (int)kchunk, partial, counters, (T*)out);
+  } else {
+    const int64_t tiles = (M + 63) / 64;
+    if (tiles > 0x7fffffff) return RQ_ERR_INVALID;
+    lora_down_mma_k<DT, WT, 4><<<dim3((unsigned)tiles, 1), 128, 0, st>>>(
+        (const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (int)Kr, partial, counters, (T*)out);
+  }
+  return check_launch();
+}
+
+// Entry used by the layer dispatcher.  `partial`/`counters` may be null (no
+// split).  Returns an RQ_* status.
+int lora_down(int dt, bool w_transposed, const void* X, int64_t M, int64_t Kr, const void* W2, int R, float pre_s,
+              bool do_pre, void* out, float* partial, int64_t partial_elems, unsigned* counters, int ncounters,
+              cudaStream_t st) {
+  if (R < 1 || R > kLoraMaxR) return RQ_ERR_INVALID;
+  if (dt == RQ_F32) {
+    const int64_t n = M * R;
+    const int64_t grid = (n + 255) / 256;
+    if (w_transposed)
+      lora_down_f32_k<true><<<(unsigned)grid, 256, 0, st>>>((const float*)X, M, Kr, (const float*)W2, R, pre_s,
+                                                            do_pre, (float*)out);
+    else
+      lora_down_f32_k<false><<<(unsigned)grid, 256, 0, st>>>((const float*)X, M, Kr, (const float*)W2, R, pre_s,
+                                                             do_pre, (float*)out);
+    return check_launch();
+  }
+  if (dt == RQ_BF16)
+    return w_transposed ? lora_down_t<RQ_BF16, true>(X, M, Kr, W2, R, pre_s, do_pre, out, partial, partial_elems,
+                                                     counters, ncounters, st)
+                        : lora_down_t<RQ_BF16, false>(X, M, Kr, W2, R, pre_s, do_pre, out, partial, partial_elems,
+                                                      counters, ncounters, st);
+  if (dt == RQ_F16)
+    return w_transposed ? lora_down_t<RQ_F16, true>(X, M, Kr, W2, R, pre_s, do_pre, out, partial, partial_elems,
+                                                    counters, ncounters, st)
+                        : lora_down_t<RQ_F16, false>(X, M, Kr, W2, R, pre_s, do_pre, out, partial, partial_elems,
+                                                     counters, ncounters, st);
+  return RQ_ERR_DTYPE;
+}
+
+}  // namespace rq

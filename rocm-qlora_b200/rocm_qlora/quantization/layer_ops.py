@@ -1,0 +1,179 @@
+"""Autograd wrappers around the fused QuantLinear(+LoRA) kernels.
+
+``QuantLinear.forward`` and ``LoRALinear.forward`` call into here; each call
+is one ``rq_linear_forward`` (and, in backward, one ``rq_linear_dx``) on the
+current CUDA stream.  The adapter gradients dA / dB are plain cuBLAS matmuls
+in the activation dtype with the same roundings as the reference's autograd
+of ``x @ A.T @ B.T * scaling`` (rocm_qlora/lora/lora_layer.py:67).
+"""
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from rocm_qlora import _native as nat
+
+
+@dataclass
+class WeightView:
+    """The quantized operand of a QuantLinear, as the C ABI takes it."""
+    fmt: int
+    q: torch.Tensor
+    scales: Optional[torch.Tensor]
+    c2: Optional[torch.Tensor]
+    c2_scales: Optional[torch.Tensor]
+    N: int
+    K: int
+    block_size: int
+
+    @property
+    def device(self) -> torch.device:
+        return self.q.device
+
+    def args(self):
+        sc = self.scales
+        return (self.fmt, self.q.data_ptr(), nat.ptr(sc), nat.dtype_code(sc.dtype) if sc is not None else 0,
+                nat.ptr(self.c2), nat.ptr(self.c2_scales), self.N, self.K, self.block_size)
+
+
+def weight_view(ql) -> WeightView:
+    """WeightView of a QuantLinear module (formats of quant_linear.py)."""
+    N, K = ql.out_features, ql.in_features
+    if ql.bits == 4:
+        if getattr(ql, "use_double_quant", False):
+            if not hasattr(ql, "c2") or not hasattr(ql, "c2_scales"):
+                raise RuntimeError(
+                    "Double quantization attributes not initialized. "
+                    "Call patch_quant_linear_for_double_quant() first.")
+            fmt = nat.W_NF4_DQ_FP8 if getattr(ql, "use_fp8_c2", True) else nat.W_NF4_DQ_INT8
+            c2 = ql.c2.reshape(-1).view(torch.uint8)
+            c2s = ql.c2_scales.reshape(-1).to(torch.float32)
+            return WeightView(fmt, ql.weight_quant.reshape(-1), None, c2.contiguous(), c2s.contiguous(), N, K,
+                              ql.block_size)
+        return WeightView(nat.W_NF4, ql.weight_quant.reshape(-1), ql.weight_scales.reshape(-1).contiguous(),
+                          None, None, N, K, ql.block_size)
+    if ql.bits == 8:
+        wq = ql.weight_quant
+        sc = ql.weight_scales.reshape(-1).contiguous()
+        if wq.dim() == 2 and sc.numel() == wq.size(0):
+            return WeightView(nat.W_INT8_ROW, wq.contiguous(), sc, None, None, N, K, ql.block_size)
+        return WeightView(nat.W_INT8, wq.reshape(-1), sc, None, None, N, K, ql.block_size)
+    raise ValueError(f"Unsupported bit depth: {ql.bits}")
+
+
+def _check_device(w: WeightView, x: torch.Tensor) -> None:
+    if not x.is_cuda:
+        raise nat.NativeUnavailable(
+            "rocm_qlora (B200 build) computes on the GPU only: move the input and the model to a CUDA device")
+    if w.q.device != x.device:
+        raise RuntimeError(f"QuantLinear buffers are on {w.q.device} but the input is on {x.device}")
+
+
+def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: Optional[torch.Tensor],
+            B: Optional[torch.Tensor], scaling: float, lora_x: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[M, N] of LoRALinear.forward (eval) over QuantLinear.forward."""
+    L = nat.lib()
+    _check_device(w, x2d)
+    dev = x2d.device
+    M = x2d.shape[0]
+    dt = nat.dtype_code(x2d.dtype)
+    r = 0 if A is None else A.shape[0]
+    y = torch.empty(M, w.N, dtype=x2d.dtype, device=dev)
+    with torch.cuda.device(dev):
+        nbytes = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
+        ws = nat.workspace(dev, nbytes)
+        nat.check(L.rq_linear_forward(*w.args(), x2d.data_ptr(), dt, M, nat.ptr(lora_x), nat.ptr(bias),
+                                      nat.dtype_code(bias.dtype) if bias is not None else 0, nat.ptr(A), nat.ptr(B),
+                                      r, float(scaling), y.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      nat.stream_ptr(dev)), "rq_linear_forward")
+    return y
+
+
+def dx(w: WeightView, dy2d: torch.Tensor, A: Optional[torch.Tensor], B: Optional[torch.Tensor],
+       scaling: float) -> torch.Tensor:
+    """dx[M, K] = rnd(rnd(dy . W) + rnd(rnd(rnd(dy*s) . B) . A))."""
+    L = nat.lib()
+    _check_device(w, dy2d)
+    dev = dy2d.device
+    M = dy2d.shape[0]
+    r = 0 if A is None else A.shape[0]
+    out = torch.empty(M, w.K, dtype=dy2d.dtype, device=dev)
+    with torch.cuda.device(dev):
+        nbytes = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
+        ws = nat.workspace(dev, nbytes)
+        nat.check(L.rq_linear_dx(*w.args(), dy2d.data_ptr(), nat.dtype_code(dy2d.dtype), M, nat.ptr(A), nat.ptr(B),
+                                 r, float(scaling), out.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
+                  "rq_linear_dx")
+    return out
+
+
+class QuantLinearFunction(torch.autograd.Function):
+    """F.linear(x, deq(W).to(x.dtype), bias) with a frozen quantized weight."""
+
+    @staticmethod
+    def forward(ctx, x, w: WeightView, bias):
+        K = x.shape[-1]
+        x2 = x.reshape(-1, K).contiguous()
+        b = bias.to(x.dtype).contiguous() if bias is not None else None
+        y = forward(w, x2, b, None, None, 1.0)
+        ctx.w = w
+        ctx.x_shape = x.shape
+        return y.view(*x.shape[:-1], w.N)
+
+    @staticmethod
+    def backward(ctx, gy):
+        w = ctx.w
+        gx = None
+        if ctx.needs_input_grad[0]:
+            gx = dx(w, gy.reshape(-1, w.N).contiguous(), None, None, 1.0).view(ctx.x_shape)
+        return gx, None, None
+
+
+class LoRAQuantFunction(torch.autograd.Function):
+    """LoRALinear.forward over a QuantLinear base in one fused kernel.
+
+    Inputs: x [..., K]; lora_A [r, K] and lora_B [N, r] (parameters, any
+    float dtype, used in x.dtype); xd = the adapter input when LoRA dropout
+    is active (else None, meaning x).  With xd given, x's gradient carries
+    only the base term and xd's gradient the adapter term, so autograd adds
+    them after the dropout backward exactly as in the reference."""
+
+    @staticmethod
+    def forward(ctx, x, lora_A, lora_B, xd, w: WeightView, bias, scaling):
+        K = x.shape[-1]
+        dt = x.dtype
+        x2 = x.reshape(-1, K).contiguous()
+        xd2 = xd.reshape(-1, K).contiguous() if xd is not None else None
+        A = lora_A.to(dt).contiguous()
+        B = lora_B.to(dt).contiguous()
+        b = bias.to(dt).contiguous() if bias is not None else None
+        y = forward(w, x2, b, A, B, scaling, lora_x=xd2)
+        ctx.save_for_backward(x2 if xd2 is None else xd2, A, B)
+        ctx.w, ctx.scaling, ctx.has_xd = w, scaling, xd is not None
+        ctx.x_shape = x.shape
+        ctx.param_dtypes = (lora_A.dtype, lora_B.dtype)
+        return y.view(*x.shape[:-1], w.N)
+
+    @staticmethod
+    def backward(ctx, gy):
+        xin, A, B = ctx.saved_tensors
+        w, s = ctx.w, ctx.scaling
+        dy = gy.reshape(-1, w.N).contiguous()
+        gx = gA = gB = gxd = None
+        need_x, need_A, need_B, need_xd = ctx.needs_input_grad[:4]
+        if need_x:
+            if ctx.has_xd:
+                gx = dx(w, dy, None, None, 1.0).view(ctx.x_shape)
+            else:
+                gx = dx(w, dy, A, B, s).view(ctx.x_shape)
+        if need_A or need_B or need_xd:
+            gu = dy * s                      # grad of (u * scaling), rounded to dt
+            gt = gu @ B                      # grad of t = x @ A.T      [M, r]
+            if need_B:
+                t = xin @ A.t()
+                gB = (gu.t() @ t).to(ctx.param_dtypes[1])
+            if need_A:
+                gA = (gt.t() @ xin).to(ctx.param_dtypes[0])
+            if need_xd and ctx.has_xd:
+                gxd = (gt @ A).view(ctx.x_shape)
+        return gx, gA, gB, gxd, None, None, None

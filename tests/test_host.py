@@ -1,0 +1,141 @@
+"""CPU-only tests of the host side: the C-ABI library loads and exports every
+symbol include/rq_b200.h declares, the Python API mirrors the reference's
+surface and validation, and nothing computes without the GPU kernels."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+import torch.nn as nn
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "rq_b200.h")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"RQ_API\s+[\w\s\*]+?\b((?:rq|launch)_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    from rocm_qlora import _native as nat
+    L = nat.load_library()
+    syms = header_symbols()
+    assert len(syms) >= 16
+    for s in syms:
+        assert hasattr(L, s), f"{s} missing from {nat.LIB_PATH}"
+    assert set(syms) == set(nat.exported_symbols())
+    out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T ((?:rq|launch)_\w+)", out))
+    assert exported == set(syms)
+
+
+def test_library_is_sm100a():
+    """The shared library carries sm_100a device code (checked from the
+    build log's target list, not by decoding the binary)."""
+    from rocm_qlora import _native as nat
+    L = nat.load_library()
+    assert L.rq_abi_version() == 1
+    mk = open(os.path.join(ROOT, "rocm-qlora_b200", "Makefile")).read()
+    assert "arch=compute_100a,code=sm_100a" in mk
+
+
+def test_status_strings():
+    from rocm_qlora import _native as nat
+    L = nat.load_library()
+    assert L.rq_status_string(0) == b"ok"
+    assert b"workspace" in L.rq_status_string(-5)
+    assert b"sm_100" in L.rq_status_string(-6)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU behaviour")
+def test_no_cpu_fallback():
+    """Without a CUDA device every compute call raises instead of computing
+    on the CPU."""
+    from rocm_qlora import _native as nat
+    from rocm_qlora.quantization import quantize_int4, dequantize_int8
+    with pytest.raises(nat.NativeUnavailable):
+        quantize_int4(torch.randn(64))
+    with pytest.raises(nat.NativeUnavailable):
+        dequantize_int8(torch.zeros(64, dtype=torch.int8), torch.ones(1))
+    from rocm_qlora import QuantLinear
+    with pytest.raises(nat.NativeUnavailable):
+        QuantLinear.from_linear(nn.Linear(64, 64), bits=4)
+
+
+def test_config_validation_and_roundtrip():
+    from rocm_qlora import RocmQLoraConfig
+    c = RocmQLoraConfig(bits=4, lora_r=16)
+    assert c.to_dict()["bits"] == 4 and c.target_modules == ["q_proj", "v_proj", "k_proj", "o_proj"]
+    assert RocmQLoraConfig.from_dict(c.to_dict()).to_dict() == c.to_dict()
+    with pytest.raises(ValueError, match="only supports 4 or 8 bits"):
+        RocmQLoraConfig(bits=3)
+
+
+def test_quantize_model_rejects_bits():
+    from rocm_qlora import quantize_model
+    with pytest.raises(ValueError, match="Only 4 and 8 bits are supported"):
+        quantize_model(nn.Linear(128, 128), bits=3)
+
+
+def test_quantlinear_constructor_buffers():
+    from rocm_qlora import QuantLinear
+    ql = QuantLinear(64, 128, bits=4)
+    names = set(dict(ql.named_buffers()))
+    assert {"weight_quant", "weight_scales", "weight_zeros", "bias"} <= names
+    assert ql.weight_quant.dtype == torch.uint8
+    assert QuantLinear(64, 128, bits=8).weight_quant.dtype == torch.int8
+    assert sum(p.numel() for p in ql.parameters()) == 0
+    assert "in=64, out=128, bits=4" in repr(ql)
+
+
+def test_lora_layer_params_without_compute():
+    from rocm_qlora import LoRALinear, QuantLinear
+    lora = LoRALinear(QuantLinear(64, 128, bits=8), r=8)
+    trainable = [n for n, p in lora.named_parameters() if p.requires_grad]
+    assert trainable == ["lora_A", "lora_B"]
+    assert lora.get_trainable_params() == 1536
+    assert torch.count_nonzero(lora.lora_B) == 0
+    assert lora.scaling == 2.0
+
+
+def test_double_quant_savings_estimate():
+    from rocm_qlora.quantization import estimate_double_quant_savings
+    s = estimate_double_quant_savings(torch.empty(4096, 4096))
+    assert 0.35 < s["bits_saved_per_param"] < 0.40
+    assert s["saved_bytes"] > 0
+
+
+def test_double_quant_state_defaults():
+    from rocm_qlora.quantization import DoubleQuantState
+    st = DoubleQuantState(W_quant=torch.zeros(1, dtype=torch.uint8), c2=torch.zeros(1), c2_scales=torch.zeros(1),
+                          original_shape=(10, 10))
+    assert st.blocksize_1 == 64 and st.blocksize_2 == 256
+
+
+def test_public_names_match_reference_surface():
+    import rocm_qlora
+    import rocm_qlora.kernels as k
+    import rocm_qlora.quantization as q
+    for name in ["quantize_model", "QuantLinear", "LoRALinear", "enable_all_kernels", "RocmQLoraConfig",
+                 "fused_dequant_int8_matmul", "fused_dequant_nf4_matmul", "get_device_info", "is_triton_available"]:
+        assert hasattr(rocm_qlora, name)
+    for name in ["quantize_int8", "dequantize_int8", "quantize_int4", "dequantize_int4", "QuantLinear",
+                 "double_quantize", "double_dequantize", "DoubleQuantState", "estimate_double_quant_savings",
+                 "patch_quant_linear_for_double_quant"]:
+        assert hasattr(q, name)
+    for name in ["get_kernel_config", "get_device_info", "is_triton_available", "fused_dequant_int8_matmul",
+                 "fused_dequant_nf4_matmul", "dequantize_nf4_triton"]:
+        assert hasattr(k, name)
+    info = k.get_device_info()
+    assert {"arch", "compute_units", "vram_gb", "wavefront_size", "triton_available"} <= set(info)
+
+
+def test_workspace_size_query():
+    from rocm_qlora import _native as nat
+    L = nat.load_library()
+    assert L.rq_linear_workspace_bytes(16, 4096, 4096, 0) == 256
+    assert L.rq_linear_workspace_bytes(16, 4096, 4096, 16) > 256
+    assert L.rq_linear_workspace_bytes(-1, 1, 1, 1) == -1
