@@ -238,11 +238,11 @@ def test_fused_matmul_entry_points():
         p, s = quantize_int4(w.flatten(), block_size=bs)
         y = fused_dequant_nf4_matmul(x, p.reshape(N, K // 2), s, block_size=bs)
         wdeq = orc.nf4_dequantize(p.cpu().numpy(), s.cpu().numpy(), 0, bs).reshape(N, K)
-        assert_matmul_close(to_f32(y), orc.quantlinear_forward(to_f32(x), wdeq, None, 1), 1)
+        assert_matmul_close(to_f32(y), orc.quantlinear_forward(to_f32(x), wdeq, None, 1), 1, roundings=1)
         q, s8 = quantize_int8(w.flatten(), block_size=bs)
         y8 = fused_dequant_int8_matmul(x, q.reshape(N, K), s8, block_size=bs)
         wdeq8 = orc.int8_dequantize(q.cpu().numpy(), s8.cpu().numpy(), 0, bs).reshape(N, K)
-        assert_matmul_close(to_f32(y8), orc.quantlinear_forward(to_f32(x), wdeq8, None, 1), 1)
+        assert_matmul_close(to_f32(y8), orc.quantlinear_forward(to_f32(x), wdeq8, None, 1), 1, roundings=1)
     x3 = torch.randn(2, 8, K, device="cuda", dtype=torch.bfloat16)
     assert fused_dequant_nf4_matmul(x3, p, s, block_size=64).shape == (2, 8, N)
 
@@ -258,7 +258,8 @@ def test_odd_shapes_exact_path():
         y = ql(x)
         assert y.shape == (3, 73)
         wdeq = oracle_wdeq(ql, 73, 37)
-        assert_matmul_close(to_f32(y), orc.quantlinear_forward(to_f32(x), wdeq, ql.bias.cpu().numpy(), 0), 0)
+        assert_matmul_close(to_f32(y), orc.quantlinear_forward(to_f32(x), wdeq, ql.bias.cpu().numpy(), 0), 0,
+                            roundings=1)
 
 
 def test_raw_abi_errors_and_drop_in_launcher():
@@ -295,7 +296,7 @@ def test_raw_abi_errors_and_drop_in_launcher():
     L.launch_int4_dequant_matmul(st, xh.data_ptr(), p.data_ptr(), sc.data_ptr(), c.data_ptr(), M, N, K, 64)
     assert L.rq_last_status() == 0
     wdeq = orc.nf4_dequantize(p.cpu().numpy(), to_bits(sc), 2).reshape(N, K)
-    assert_matmul_close(to_f32(c), orc.quantlinear_forward(to_f32(xh), wdeq, None, 2), 2)
+    assert_matmul_close(to_f32(c), orc.quantlinear_forward(to_f32(xh), wdeq, None, 2), 2, roundings=1)
 
 
 def test_cuda_graph_capture_decode():

@@ -2,14 +2,20 @@
 
 The north-star bar is: max-abs error <= 1e-2 x RMS(reference output), for bf16
 inputs with fp32 accumulation.  Outputs are stored in the activation dtype, so
-two correct implementations that sum in different orders can land one output
-ulp apart wherever the fp32 sum sits next to a rounding boundary; for bf16 one
-ulp exceeds 1e-2 x RMS as soon as |y| >= 2 x RMS.  The check is therefore
+two correct implementations whose fp32 sums differ slightly (summation order,
+or where in the chain a weight is rounded) land one output ulp apart wherever
+the sum sits next to a rounding boundary -- and the reference rounds more
+than once: LoRALinear rounds the base output, then rounds again after adding
+the adapter term, so a one-ulp move of the base can become two when the
+adapter term is an exact half ulp (ties-to-even).  For bf16 one ulp exceeds
+1e-2 x RMS as soon as |y| >= 2 x RMS.  The check is therefore
 
-    |y - y_ref| <= 1e-2 * rms(y_ref) + ulp(y_ref)     (elementwise)
+    |y - y_ref| <= 1e-2 * rms(y_ref) + roundings * ulp(y_ref)   (elementwise)
 
-where ulp is one unit in the last place of the stored dtype at y_ref (0 for
-fp32).  ``matmul_error`` also reports the plain max-abs / RMS figure.
+with `roundings` the number of output roundings after the accumulation in
+the reference's op sequence (1 for QuantLinear alone, 2 with the adapter),
+ulp = one unit in the last place of the stored dtype at y_ref (0 for fp32).
+``matmul_error`` reports the plain max-abs / RMS figure alongside.
 """
 import numpy as np
 
@@ -36,16 +42,16 @@ def matmul_error(y, y_ref):
     return err, rms
 
 
-def assert_matmul_close(y, y_ref, dtype):
+def assert_matmul_close(y, y_ref, dtype, roundings=2):
     y = np.asarray(y, np.float64)
     y_ref = np.asarray(y_ref, np.float64)
     assert y.shape == y_ref.shape, (y.shape, y_ref.shape)
     assert np.all(np.isfinite(y)), "non-finite output"
     err, rms = matmul_error(y, y_ref)
-    bound = RTOL_RMS * rms + ulp(y_ref, dtype)
+    bound = RTOL_RMS * rms + roundings * ulp(y_ref, dtype)
     bad = np.abs(y - y_ref) > bound
     if bad.any():
         i = np.argmax(np.abs(y - y_ref) - bound)
         raise AssertionError(
-            f"{int(bad.sum())}/{y.size} outputs outside 1e-2*RMS + 1 ulp: max-abs {err:.4g}, "
+            f"{int(bad.sum())}/{y.size} outputs outside 1e-2*RMS + {roundings} ulp: max-abs {err:.4g}, "
             f"rms {rms:.4g}; worst at flat {i}: {y.reshape(-1)[i]!r} vs {y_ref.reshape(-1)[i]!r}")
