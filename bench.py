@@ -1,0 +1,476 @@
+"""Benchmark of the B200 QuantLinear+LoRA hot path (one JSON line on rank 0).
+
+Workload (the decode GEMV sweep): Llama-2-7B-shaped
+projections W[N, K] in {4096x4096, 11008x4096, 4096x11008}, bf16 N(0, 0.02)
+weights quantized to NF4 with double-quantized scales (block 64, fp8
+second level over 256 blocks), X in {1, 4, 16} x K bf16 N(0, 1), LoRA r=16
+alpha=32 with B ~ N(0, 0.01).  One step = the nine LoRALinear forwards of
+the sweep.  Metric: HBM GB/s of algorithmic bytes (SURVEY 8d formula:
+N*K/2 + nb + 4*ceil(nb/256) + 2MK + 2MN + 2r(K+N) per call).
+
+The weight set is replicated over >= 512 MB of distinct copies and each step
+reads the next copy, so every call streams its weights from HBM (the 126 MB
+L2 cannot hold the rotation).  Steps are replayed from CUDA graphs (one per
+copy) and timed with CUDA events; multi-GPU runs time the max over ranks.
+
+Arms:
+  python bench.py [--gpus N] [--steps K] [--warmup W]   the B200 kernels
+  python bench.py --impl reference ...                  the reference's CPU
+      path as restated by the oracle (C dequantize + numpy matmul), on this
+      host's cores, over a bounded sample of the same workload.
+With N > 1 (torchrun), each rank holds a column shard: the sweep's layers
+have N times the output features, every rank runs its [N_shape, K] shard,
+and Y is all-gathered over NCCL (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "rocm-qlora_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008)]
+MS = [1, 4, 16]
+R, ALPHA = 16, 32
+ROTATE_BYTES = 512 << 20
+METRIC = "NF4 QuantLinear+LoRA decode HBM GB/s (configs[1] sweep)"
+
+
+def algo_bytes(N, K, M, r, lora=True):
+    nb = N * K // 64
+    b = N * K // 2 + nb + 4 * ((nb + 255) // 256) + 2 * M * K + 2 * M * N
+    return b + (2 * r * (K + N) if lora else 0)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------- clock sampler
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{index}.csv")
+
+    def __enter__(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# -------------------------------------------------------------- B200 arm
+def build_layers(world: int, rank: int, device):
+    """Quantized LoRA layers of the sweep (this rank's shard) and copies."""
+    import torch.nn as nn
+    from rocm_qlora import LoRALinear, QuantLinear
+    from tests.inputs import layer_inputs
+    layers = []
+    for si, (N, K) in enumerate(SHAPES):
+        inp = layer_inputs(N, K, 1, sigma=0.02, r=R, alpha=ALPHA, seed=100 + si + 17 * rank)
+        lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=device)
+        with torch.no_grad():
+            lin.weight.copy_(inp.W.to(device))
+        ql = QuantLinear.from_linear(lin, bits=4)
+        ql.enable_double_quant()
+        lora = LoRALinear(ql, r=R, lora_alpha=ALPHA).to(device).eval()
+        with torch.no_grad():
+            lora.lora_A.copy_(inp.A)
+            lora.lora_B.copy_(inp.B)
+        layers.append(lora)
+    return layers
+
+
+def clone_weights(layers, copies):
+    """`copies` independent copies of each layer's quantized buffers."""
+    from rocm_qlora.quantization.layer_ops import weight_view
+    sets = []
+    for _ in range(copies):
+        views = []
+        for lora in layers:
+            w = weight_view(lora.base_layer)
+            views.append(type(w)(w.fmt, w.q.clone(), None, w.c2.clone(), w.c2_scales.clone(), w.N, w.K,
+                                 w.block_size))
+        sets.append(views)
+    return sets
+
+
+def run_ours(args, rank, world, device):
+    import torch.distributed as dist
+    from rocm_qlora.quantization import layer_ops
+    hbm_peak, peak_kind = peaks()
+    layers = build_layers(world, rank, device)
+    per_set = sum(lo.base_layer.weight_quant.numel() + lo.base_layer.c2.numel() for lo in layers)
+    copies = max(2, -(-ROTATE_BYTES // per_set))
+    wsets = clone_weights(layers, copies)
+    g = torch.Generator().manual_seed(7)
+    xs = {(si, M): torch.randn(M, K, generator=g).to(torch.bfloat16).to(device)
+          for si, (N, K) in enumerate(SHAPES) for M in MS}
+    A = [lo.lora_A.detach().to(torch.bfloat16).contiguous() for lo in layers]
+    B = [lo.lora_B.detach().to(torch.bfloat16).contiguous() for lo in layers]
+    calls = [(si, M) for si in range(len(SHAPES)) for M in MS]
+
+    gather_out = {}
+    if world > 1:
+        for si, (N, K) in enumerate(SHAPES):
+            for M in MS:
+                gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
+
+    def step(c, lora=True):
+        for si, M in calls:
+            w = wsets[c][si]
+            if lora:
+                y = layer_ops.forward(w, xs[(si, M)], None, A[si], B[si], ALPHA / R)
+            else:
+                y = layer_ops.forward(w, xs[(si, M)], None, None, None, 1.0)
+            if world > 1:
+                dist.all_gather_into_tensor(gather_out[(si, M)], y)
+
+    def capture(lora):
+        graphs = []
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            for c in range(copies):
+                step(c, lora)
+        torch.cuda.current_stream(device).wait_stream(s)
+        torch.cuda.synchronize(device)
+        for c in range(copies):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step(c, lora)
+            graphs.append(gr)
+        return graphs
+
+    use_graphs = True
+    graphs = capture(True)
+
+    def run_steps(n, start, lora=True, gr=None):
+        for i in range(n):
+            c = (start + i) % copies
+            if gr is not None:
+                gr[c].replay()
+            else:
+                step(c, lora)
+
+    def timed(n, lora=True, gr=None):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        st = torch.cuda.current_stream(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        run_steps(n, 0, lora, gr)
+        e1.record(st)
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    run_steps(args.warmup, 0, True, graphs)
+    with ClockSampler(device.index) as clk:
+        ms = timed(args.steps, True, graphs)
+    clocks = clk.summary()
+    step_bytes = sum(algo_bytes(SHAPES[si][0], SHAPES[si][1], M, R) for si, M in calls)
+    value = step_bytes * args.steps * world / (ms / 1e3) / 1e9
+
+    # roofline of the dominant kernel: the fused GEMV alone (no adapter)
+    gemv_graphs = capture(False)
+    run_steps(max(3, args.warmup), 0, False, gemv_graphs)
+    ms_g = timed(args.steps, False, gemv_graphs)
+    gemv_bytes = sum(algo_bytes(SHAPES[si][0], SHAPES[si][1], M, R, lora=False) for si, M in calls)
+    n_launch = args.steps * len(calls)
+    achieved = gemv_bytes * args.steps / (ms_g / 1e3) / 1e9
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "gemv_decode_traffic.json")
+    if os.path.exists(tfile):
+        try:
+            traffic = json.load(open(tfile)).get("bytes_per_launch_avg")
+        except Exception:
+            traffic = None
+
+    # graphs that hold NCCL calls are released before the process group goes
+    del graphs, gemv_graphs
+    torch.cuda.synchronize(device)
+
+    # end to end through the public API with host buffers
+    e2e = run_e2e(args, rotated_modules(layers, wsets), device, world)
+
+    # CPU baseline on rank 0 (bounded sample of the same workload)
+    cpu = cpu_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,.) tensors)",
+            "config": {"workload": "configs[1]: decode GEMV sweep, W in 4096x4096 / 11008x4096 / 4096x11008 "
+                                   "NF4 + double-quant, M in {1,4,16}, LoRA r16 a32",
+                       "model": "Llama-2-7B-shaped projections", "global_batch": MS, "seq_len": 1,
+                       "parallelism": f"column-shard x{world}" if world > 1 else "single GPU",
+                       "l2": f"{copies} rotating weight copies ({copies * per_set / 2**20:.0f} MiB) > 126 MB L2",
+                       "graphs": use_graphs},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "gemv_k (fused NF4-DQ dequant GEMV, no adapter)",
+                         "launches": n_launch, "us_per_launch": round(ms_g * 1e3 / n_launch, 3)},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * len(calls) * 2,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def rotated_modules(layers, wsets):
+    """LoRALinear modules sharing the adapters of `layers` but reading the
+    rotated weight copies, so the public-API leg streams from HBM too."""
+    import copy
+    mods = []
+    for views in wsets:
+        row = []
+        for lora, w in zip(layers, views):
+            ql = copy.copy(lora.base_layer)
+            ql._buffers = dict(lora.base_layer._buffers)
+            ql._buffers["weight_quant"] = w.q
+            ql._buffers["c2"] = w.c2.view(lora.base_layer.c2.dtype)
+            ql._buffers["c2_scales"] = w.c2_scales
+            lo = copy.copy(lora)
+            lo._modules = dict(lora._modules)
+            lo._modules["base_layer"] = ql
+            row.append(lo)
+        mods.append(row)
+    return mods
+
+
+def run_e2e(args, mods, device, world):
+    """Public-API timing: pinned host X -> device, LoRALinear.forward, Y -> host."""
+    g = torch.Generator().manual_seed(9)
+    hx = {(si, M): torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory()
+          for si, (N, K) in enumerate(SHAPES) for M in MS}
+    hy = {(si, M): torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+          for si, (N, K) in enumerate(SHAPES) for M in MS}
+    calls = [(si, M) for si in range(len(SHAPES)) for M in MS]
+
+    def one(c):
+        with torch.no_grad():
+            for si, M in calls:
+                x = hx[(si, M)].to(device, non_blocking=True)
+                y = mods[c % len(mods)][si](x)
+                hy[(si, M)].copy_(y, non_blocking=True)
+
+    for i in range(max(3, args.warmup)):
+        one(i)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one(i)
+    torch.cuda.synchronize(device)
+    dt = time.perf_counter() - t0
+    step_bytes = sum(algo_bytes(SHAPES[si][0], SHAPES[si][1], M, R) for si, M in calls)
+    h2d = sum(M * SHAPES[si][1] * 2 for si, M in calls)
+    d2h = sum(M * SHAPES[si][0] * 2 for si, M in calls)
+    return {"value": round(step_bytes * args.steps / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "note": "eager LoRALinear.forward per call, wall clock, no CUDA graph"}
+
+
+# --------------------------------------------------------- CPU reference
+def _cpu_layers():
+    """The sweep's quantized layers on the host: codes and double-quant
+    scales from the C oracle (bit-exact with the reference), adapters."""
+    import numpy as np
+    from oracle import oracle as orc
+    from tests.inputs import layer_inputs
+    out = []
+    for si, (N, K) in enumerate(SHAPES):
+        inp = layer_inputs(N, K, 1, sigma=0.02, r=R, alpha=ALPHA, seed=100 + si)
+        wb = inp.W.view(torch.int16).numpy().view(np.uint16).reshape(-1)
+        packed, scales = orc.nf4_quantize(wb, orc.BF16, 64)
+        c2, c2s = orc.enable_double_quant(packed, scales, orc.BF16, N * K)
+        out.append((N, K, torch.from_numpy(packed), torch.from_numpy(c2), torch.from_numpy(c2s), inp.A, inp.B))
+    return out
+
+
+def cpu_baseline(args, layers=None, seconds=12.0):
+    """The reference's eager CPU path (torch ops restated in
+    oracle/torch_port.py) timed on this host with all its threads."""
+    from oracle import torch_port
+    torch.set_num_threads(os.cpu_count() or 1)
+    layers = layers or _cpu_layers()
+    g = torch.Generator().manual_seed(3)
+    calls = [(si, M) for si in range(len(SHAPES)) for M in MS]
+    done_bytes, t_total, n = 0, 0.0, 0
+    while t_total < seconds or n < len(calls):
+        si, M = calls[n % len(calls)]
+        N, K, packed, c2, c2s, A, B = layers[si]
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            torch_port.loralinear_forward_dq(x, packed, c2, c2s, N, K, A, B, ALPHA / R)
+        t_total += time.perf_counter() - t0
+        done_bytes += algo_bytes(N, K, M, R)
+        n += 1
+    return {"value": round(done_bytes / t_total / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} LoRALinear forwards of the sweep (torch CPU eager ops of the reference, "
+                      f"{t_total:.1f} s)"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the CPU port on rank 0; other ranks exit."""
+    if rank != 0:
+        return
+    layers = _cpu_layers()
+    for _ in range(args.warmup):
+        cpu_baseline(args, layers, seconds=0.0)
+    t0 = time.perf_counter()
+    vals = [cpu_baseline(args, layers, seconds=0.0) for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    v = statistics.median(x["value"] for x in vals)
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall * 1e3 / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,.) tensors)",
+            "impl": "reference",
+            "config": {"workload": "configs[1]: decode GEMV sweep (one step = one pass of the 9 calls)",
+                       "model": "Llama-2-7B-shaped projections", "global_batch": MS, "seq_len": 1,
+                       "parallelism": "host CPU"},
+            "cpu_baseline": {**vals[-1], "value": v},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_case(args, device):
+    """--case decode:N:K:M[:r] or prefill:N:K:M[:r] -- one layer call repeated
+    (for profilers; prints the mean CUDA-event time per call)."""
+    import torch.nn as nn
+    from rocm_qlora import LoRALinear, QuantLinear
+    from tests.inputs import layer_inputs
+    parts = args.case.split(":")
+    kind, N, K, M = parts[0], int(parts[1]), int(parts[2]), int(parts[3])
+    r = int(parts[4]) if len(parts) > 4 else R
+    inp = layer_inputs(N, K, M, sigma=0.02, r=max(r, 1), alpha=2 * max(r, 1), seed=1, with_dy=kind == "dx")
+    lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=device)
+    with torch.no_grad():
+        lin.weight.copy_(inp.W.to(device))
+    ql = QuantLinear.from_linear(lin, bits=4)
+    ql.enable_double_quant()
+    lora = LoRALinear(ql, r=max(r, 1), lora_alpha=2 * max(r, 1)).to(device).eval()
+    with torch.no_grad():
+        lora.lora_A.copy_(inp.A)
+        lora.lora_B.copy_(inp.B)
+    from rocm_qlora.quantization import layer_ops
+    w = ql.weight_view()
+    x = inp.X.to(device)
+    A = lora.lora_A.detach().bfloat16() if r > 0 else None
+    B = lora.lora_B.detach().bfloat16() if r > 0 else None
+    if kind == "dx":
+        dy = inp.dY.to(device)
+        fn = lambda: layer_ops.dx(w, dy, A, B, 2.0)  # noqa: E731
+    else:
+        fn = lambda: layer_ops.forward(w, x, None, A, B, 2.0)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "us_per_call": e0.elapsed_time(e1) * 1e3 / args.steps}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="single-layer run for profiling, e.g. decode:11008:4096:16")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if args.case:
+        run_case(args, device)
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        run_ours(args, rank, world, device)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

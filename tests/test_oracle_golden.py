@@ -162,3 +162,22 @@ def test_config1_codes_and_scales_pinned():
     wdeq = orc.nf4_dequantize(packed, scales, orc.F32).reshape(4096, 4096)
     y = orc.loralinear_forward(c1.X.numpy(), wdeq, None, c1.A.numpy(), c1.B.numpy(), c1.scaling, orc.F32)
     assert_matmul_close(y, z["y"], orc.F32)
+
+
+def test_torch_port_matches_reference_layer():
+    """oracle/torch_port.py (the timed CPU baseline) reproduces the
+    reference's double-quant layer output on the golden case."""
+    import torch
+    from oracle import torch_port
+    z = load("layers.npz")
+    name = "nf4dq_bf16"
+    c = _layer_case(z, name)
+    N, K, M = c["N"], c["K"], c["M"]
+    packed, scales = orc.nf4_quantize(z[f"{name}/w"], c["wdt"], 64)
+    c2, c2s = orc.enable_double_quant(packed, scales, c["wdt"], N * K)
+    x = torch.from_numpy(z[f"{name}/x"].astype(np.int16)).view(torch.bfloat16).reshape(M, K)
+    A = torch.from_numpy(z[f"{name}/A"].reshape(c["r"], K))
+    B = torch.from_numpy(z[f"{name}/B"].reshape(N, c["r"]))
+    y = torch_port.loralinear_forward_dq(x, torch.from_numpy(packed), torch.from_numpy(c2), torch.from_numpy(c2s),
+                                         N, K, A, B, c["alpha"] / c["r"])
+    assert_matmul_close(y.float().numpy(), orc.to_f32(z[f"{name}/y"], 1).reshape(M, N), 1)
