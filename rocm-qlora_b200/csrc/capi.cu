@@ -5,6 +5,9 @@
 // stream.  Nothing here allocates device memory.
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <vector>
+
 #include "rq_internal.h"
 
 namespace rq {
@@ -13,6 +16,28 @@ static thread_local int g_last_cuda_error = 0;
 static thread_local int g_last_status = 0;
 
 void set_cuda_error(cudaError_t e) { g_last_cuda_error = (int)e; }
+
+int ensure_smem_limit(const void* kernel, size_t bytes) {
+  struct Entry {
+    const void* k;
+    int dev;
+    size_t bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : done)
+    if (e.k == kernel && e.dev == dev && e.bytes >= bytes) return RQ_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return RQ_ERR_CUDA;
+  }
+  done.push_back({kernel, dev, bytes});
+  return RQ_OK;
+}
 
 static int device_ok() {
   static int cache[64];  // 0 unknown, 1 ok, -1 not sm_100

@@ -51,9 +51,10 @@ template <> struct Mma16816<RQ_F16> {
   }
 };
 
-constexpr int kGemvWarps = 16;
+constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kGemvNT = 8;  // n-tiles of 8 rows held per warp (64 rows)
+constexpr int kGemvNT = 8;        // n-tiles of 8 rows held per warp (64 rows)
+constexpr int kGemvStageU = 16;   // scale loads issued per thread before use
 
 struct GemvArgs {
   QWeight w;
@@ -70,15 +71,24 @@ struct GemvArgs {
   int grid;
 };
 
+// Shared-memory table entry of code byte v for lane `lane`: the two levels
+// of the byte (low nibble = even k) as a packed 16-bit pair.  32 copies, one
+// per bank, so a warp's 32 lookups never conflict.
+__device__ __forceinline__ uint32_t lut_get(uint32_t lut_lane_base, uint32_t v) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(lut_lane_base + (v << 7)));
+  return r;
+}
+
 // WK: 0 = NF4 family (table lookup, per-block scale), 1 = INT8 blockwise,
 //     2 = INT8 per-row.  MT: 8 (M <= 8) or 16.
 template <int DT, int WK, int MT>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
   using T = typename DType<DT>::T;
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int64_t N = p.w.N, K = p.w.K, M = p.M;
-  const int64_t nbk = K / 64;
+  const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
+  const int nbk = K / 64;
   const int CH = p.chunk_rows;
   const int SCS = CH + 2;  // scale-table row stride (floats)
 
@@ -86,6 +96,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
   float* sc = reinterpret_cast<float*>(smem + (WK == 0 ? 256 * 32 * 4 : 0));
   float4* red = reinterpret_cast<float4*>(reinterpret_cast<unsigned char*>(sc) +
                                           (WK != 2 ? ((nbk * SCS * 4 + 15) / 16) * 16 : 0));
+  T* tl = reinterpret_cast<T*>(red + kGemvWarps * kGemvNT * 32);  // staged x.A^T [M, r]
 
   if constexpr (WK == 0) {
     for (int i = tid; i < 256 * 32; i += kGemvThreads) {
@@ -93,26 +104,105 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
       lut[i] = pack2<DT>(kNF4[v & 15], kNF4[v >> 4]);
     }
   }
+  if (p.r > 0) {
+    const T* td = static_cast<const T*>(p.tdown);
+    for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
+  }
+  const uint32_t lut_lane = (uint32_t)__cvta_generic_to_shared(lut) + lane * 4;
 
-  const int64_t r_begin = N * blockIdx.x / p.grid;
-  const int64_t r_end = N * (blockIdx.x + 1) / p.grid;
-  const int64_t kb0 = nbk * warp / kGemvWarps, kb1 = nbk * (warp + 1) / kGemvWarps;
+  const int r_begin = (int)((int64_t)N * blockIdx.x / p.grid);
+  const int r_end = (int)((int64_t)N * (blockIdx.x + 1) / p.grid);
+  const int kb0 = nbk * warp / kGemvWarps, kb1 = nbk * (warp + 1) / kGemvWarps;
   const uint8_t* qb = static_cast<const uint8_t*>(p.w.q);
   const T* xp = static_cast<const T*>(p.x);
   const bool rowa = g < M, rowb = (MT == 16) && (g + 8 < M);
-  const T* xa = xp + (rowa ? g : 0) * K;
-  const T* xb = xp + (rowb ? g + 8 : 0) * K;
+  const T* xa = xp + (size_t)(rowa ? g : 0) * K + t * 16;
+  const T* xb = xp + (size_t)(rowb ? g + 8 : 0) * K + t * 16;
+  constexpr int CW = (WK == 0) ? 2 : 4;   // 32-bit words of codes per lane per n-tile per block
+  constexpr int RB = (WK == 0) ? 32 : 64; // code bytes per row per block
 
-  for (int64_t c0 = r_begin; c0 < r_end; c0 += CH) {
-    const int R = (int)(r_end - c0 < CH ? r_end - c0 : CH);
+  for (int c0 = r_begin; c0 < r_end; c0 += CH) {
+    const int R = r_end - c0 < CH ? r_end - c0 : CH;
     const int ntiles = (R + 7) >> 3;
-    if constexpr (WK != 2) {
-      for (int64_t i = tid; i < (int64_t)R * nbk; i += kGemvThreads) {
-        const int64_t rl = i / nbk, b = i % nbk;
-        sc[b * SCS + rl] = block_scale(p.w, (c0 + rl) * nbk + b);
+    // per-lane byte offsets of this lane's weight row in each n-tile
+    uint32_t roff[kGemvNT];
+#pragma unroll
+    for (int nt = 0; nt < kGemvNT; ++nt) {
+      const int rl = nt * 8 + g;
+      roff[nt] = rl < R ? (uint32_t)((c0 + rl) * (uint32_t)(K / 64) * RB) + t * (RB / 4) : 0xFFFFFFFFu;
+    }
+    uint32_t cur[kGemvNT][CW];
+    auto load_codes = [&](int b, uint32_t (&dst)[kGemvNT][CW]) {
+#pragma unroll
+      for (int nt = 0; nt < kGemvNT; ++nt) {
+        if (nt < ntiles && roff[nt] != 0xFFFFFFFFu) {
+          const unsigned char* src = qb + roff[nt] + (uint32_t)b * RB;
+          if constexpr (WK == 0) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src));
+            dst[nt][0] = v.x, dst[nt][1] = v.y;
+          } else {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
+            dst[nt][0] = v.x, dst[nt][1] = v.y, dst[nt][2] = v.z, dst[nt][3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < CW; ++i) dst[nt][i] = 0u;
+        }
       }
-      for (int64_t i = tid; i < (int64_t)(CH - R) * nbk; i += kGemvThreads) {
-        const int64_t rl = R + i / nbk, b = i % nbk;
+    };
+    uint32_t xc[16];
+    auto load_x = [&](int b, uint32_t (&dst)[16]) {
+      if (rowa) {
+        const uint4* s = reinterpret_cast<const uint4*>(xa + b * 64);
+        const uint4 u0 = __ldg(s), u1 = __ldg(s + 1);
+        dst[0] = u0.x, dst[1] = u0.y, dst[2] = u0.z, dst[3] = u0.w, dst[4] = u1.x, dst[5] = u1.y, dst[6] = u1.z,
+        dst[7] = u1.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = 0u;
+      }
+      if (rowb) {
+        const uint4* s = reinterpret_cast<const uint4*>(xb + b * 64);
+        const uint4 u0 = __ldg(s), u1 = __ldg(s + 1);
+        dst[8] = u0.x, dst[9] = u0.y, dst[10] = u0.z, dst[11] = u0.w, dst[12] = u1.x, dst[13] = u1.y,
+        dst[14] = u1.z, dst[15] = u1.w;
+      } else {
+#pragma unroll
+        for (int i = 8; i < 16; ++i) dst[i] = 0u;
+      }
+    };
+    // first block's operands go out before the scale staging so their
+    // latency overlaps it
+    // NF4 prefetches one block ahead; INT8 (twice the code bytes, and the
+    // registers to match) loads each block in place
+    constexpr bool kPrefetchCodes = (WK == 0);
+    if (kb0 < kb1) {
+      if (kPrefetchCodes) load_codes(kb0, cur);
+      load_x(kb0, xc);
+    }
+    if constexpr (WK != 2) {
+      // scales of rows c0..c0+R-1: a contiguous run of R*nbk blocks; all
+      // loads of a round are issued before any is used
+      const int total = R * nbk;
+      const int64_t gbase = (int64_t)c0 * nbk;
+      for (int base = tid; base < total; base += kGemvThreads * kGemvStageU) {
+        float v[kGemvStageU];
+#pragma unroll
+        for (int u = 0; u < kGemvStageU; ++u) {
+          const int idx = base + u * kGemvThreads;
+          v[u] = idx < total ? block_scale(p.w, gbase + idx) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kGemvStageU; ++u) {
+          const int idx = base + u * kGemvThreads;
+          if (idx < total) {
+            const int rl = idx / nbk, b = idx - rl * nbk;
+            sc[b * SCS + rl] = v[u];
+          }
+        }
+      }
+      for (int idx = tid; idx < (CH - R) * nbk; idx += kGemvThreads) {
+        const int rl = R + idx / nbk, b = idx % nbk;
         sc[b * SCS + rl] = 0.0f;
       }
     }
@@ -122,65 +212,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
 #pragma unroll
     for (int i = 0; i < kGemvNT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
 
-    // code bytes per lane per n-tile per block: NF4 8 bytes, INT8 16 bytes
-    constexpr int CW = (WK == 0) ? 2 : 4;  // 32-bit words
-    uint32_t cur[kGemvNT][CW];
-    auto load_codes = [&](int64_t b, uint32_t (&dst)[kGemvNT][CW]) {
-#pragma unroll
-      for (int nt = 0; nt < kGemvNT; ++nt) {
-        const int rl = nt * 8 + g;
-        if (nt < ntiles && rl < R) {
-          const int64_t row = c0 + rl;
-          if constexpr (WK == 0) {
-            const uint2 v = __ldg(reinterpret_cast<const uint2*>(qb + row * (K / 2) + b * 32 + t * 8));
-            dst[nt][0] = v.x;
-            dst[nt][1] = v.y;
-          } else {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(qb + row * K + b * 64 + t * 16));
-            dst[nt][0] = v.x;
-            dst[nt][1] = v.y;
-            dst[nt][2] = v.z;
-            dst[nt][3] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < CW; ++i) dst[nt][i] = 0u;
-        }
-      }
-    };
-    // NF4: prefetch the next block's codes; INT8 (twice the bytes) loads in place
-    constexpr bool kPrefetch = (WK == 0);
-    if (kPrefetch && kb0 < kb1) load_codes(kb0, cur);
-
-    for (int64_t b = kb0; b < kb1; ++b) {
+    for (int b = kb0; b < kb1; ++b) {
       uint32_t nxt[kGemvNT][CW];
-      if (kPrefetch) {
-        if (b + 1 < kb1) load_codes(b + 1, nxt);
-      } else {
-        load_codes(b, cur);
+      uint32_t xn[16];
+      const bool more = b + 1 < kb1;
+      if (more) {
+        if (kPrefetchCodes) load_codes(b + 1, nxt);
+        load_x(b + 1, xn);
       }
-      // X fragments: 16 consecutive k per lane, rows g and g+8
-      uint32_t xa_r[8], xb_r[8];
-      {
-        if (rowa) {
-          const uint4* s = reinterpret_cast<const uint4*>(xa + b * 64 + t * 16);
-          const uint4 u0 = __ldg(s), u1 = __ldg(s + 1);
-          xa_r[0] = u0.x, xa_r[1] = u0.y, xa_r[2] = u0.z, xa_r[3] = u0.w;
-          xa_r[4] = u1.x, xa_r[5] = u1.y, xa_r[6] = u1.z, xa_r[7] = u1.w;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xa_r[i] = 0u;
-        }
-        if (rowb) {
-          const uint4* s = reinterpret_cast<const uint4*>(xb + b * 64 + t * 16);
-          const uint4 u0 = __ldg(s), u1 = __ldg(s + 1);
-          xb_r[0] = u0.x, xb_r[1] = u0.y, xb_r[2] = u0.z, xb_r[3] = u0.w;
-          xb_r[4] = u1.x, xb_r[5] = u1.y, xb_r[6] = u1.z, xb_r[7] = u1.w;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xb_r[i] = 0u;
-        }
-      }
+      if (!kPrefetchCodes) load_codes(b, cur);
 #pragma unroll
       for (int nt = 0; nt < kGemvNT; ++nt) {
         if (nt < ntiles) {
@@ -190,19 +230,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
             uint32_t b0, b1;
             if constexpr (WK == 0) {
               const uint32_t word = cur[nt][j >> 1];
-              const uint32_t v0 = (word >> (16 * (j & 1))) & 0xFFu;
-              const uint32_t v1 = (word >> (16 * (j & 1) + 8)) & 0xFFu;
-              b0 = lut[(v0 << 5) | lane];
-              b1 = lut[(v1 << 5) | lane];
+              const int sh = 16 * (j & 1);
+              b0 = lut_get(lut_lane, (word >> sh) & 0xFFu);
+              b1 = lut_get(lut_lane, (word >> (sh + 8)) & 0xFFu);
             } else {
               const uint32_t word = cur[nt][j];
               b0 = pack2<DT>((float)(int8_t)(word & 0xFF), (float)(int8_t)((word >> 8) & 0xFF));
               b1 = pack2<DT>((float)(int8_t)((word >> 16) & 0xFF), (float)(int8_t)(word >> 24));
             }
             if constexpr (WK == 2)
-              Mma16816<DT>::run(acc[nt], xa_r[2 * j], xb_r[2 * j], xa_r[2 * j + 1], xb_r[2 * j + 1], b0, b1);
+              Mma16816<DT>::run(acc[nt], xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
             else
-              Mma16816<DT>::run(part, xa_r[2 * j], xb_r[2 * j], xa_r[2 * j + 1], xb_r[2 * j + 1], b0, b1);
+              Mma16816<DT>::run(part, xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
           }
           if constexpr (WK != 2) {
             const float2 s2 = *reinterpret_cast<const float2*>(&sc[b * SCS + nt * 8 + 2 * t]);
@@ -213,21 +252,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
           }
         }
       }
-      if (kPrefetch && b + 1 < kb1) {
+      if (more) {
+        if (kPrefetchCodes) {
 #pragma unroll
-        for (int nt = 0; nt < kGemvNT; ++nt)
+          for (int nt = 0; nt < kGemvNT; ++nt)
 #pragma unroll
-          for (int i = 0; i < CW; ++i) cur[nt][i] = nxt[nt][i];
+            for (int i = 0; i < CW; ++i) cur[nt][i] = nxt[nt][i];
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xc[i] = xn[i];
       }
     }
 
 #pragma unroll
     for (int nt = 0; nt < kGemvNT; ++nt)
-      if (nt < ntiles) red[(warp * kGemvNT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+      if (nt < ntiles)
+        red[(warp * kGemvNT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
     __syncthreads();
 
     const bool has_bias = p.bias != nullptr, has_lora = p.r > 0;
-    const T* td = static_cast<const T*>(p.tdown);
     const T* lb = static_cast<const T*>(p.lora_b);
     T* y = static_cast<T*>(p.y);
     for (int o = tid; o < CH * MT; o += kGemvThreads) {
@@ -236,19 +279,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_k(const GemvArgs p) {
       const int nt = nl >> 3, cc = nl & 7, tt = cc >> 1, e = cc & 1;
       const int ln = (m & 7) * 4 + tt, comp = (m >> 3) * 2 + e;
       float sum = 0.0f;
-#pragma unroll 4
+#pragma unroll
       for (int w = 0; w < kGemvWarps; ++w) {
         const float* rv = reinterpret_cast<const float*>(&red[(w * kGemvNT + nt) * 32 + ln]);
         sum += rv[comp];
       }
-      const int64_t row = c0 + nl;
+      const int row = c0 + nl;
       if constexpr (WK == 2) sum *= load_scalar(p.w.scales, p.w.sdt, row);
       float u = 0.0f;
-      if (has_lora)
-        for (int j = 0; j < p.r; ++j)
-          u = fmaf(DType<DT>::to_f32(td[m * p.r + j]), DType<DT>::to_f32(lb[row * p.r + j]), u);
+      if (has_lora) {
+        const T* brow = lb + (size_t)row * p.r;
+        const T* trow = tl + m * p.r;
+#pragma unroll 8
+        for (int j = 0; j < p.r; ++j) u = fmaf(DType<DT>::to_f32(trow[j]), DType<DT>::to_f32(__ldg(brow + j)), u);
+      }
       const float bv = has_bias ? load_scalar(p.bias, p.bdt, row) : 0.0f;
-      y[m * N + row] = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, u, has_lora, p.s));
+      y[(size_t)m * N + row] = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, u, has_lora, p.s));
     }
     __syncthreads();
   }
@@ -267,12 +313,13 @@ static int num_sms() {
   return cached[dev];
 }
 
-// Shared memory the GEMV needs for this K and chunk height.
-static size_t gemv_smem(int wk, int64_t K, int chunk) {
+// Shared memory the GEMV needs for this K, chunk height and adapter size.
+static size_t gemv_smem(int wk, int64_t K, int chunk, int64_t M, int r) {
   size_t s = 0;
   if (wk == 0) s += 256 * 32 * 4;
   if (wk != 2) s += ((size_t)(K / 64) * (chunk + 2) * 4 + 15) / 16 * 16;
   s += (size_t)kGemvWarps * kGemvNT * 32 * 16;
+  s += (size_t)M * r * 2;
   return s;
 }
 
@@ -282,17 +329,15 @@ bool gemv_supported(const LinearArgs& a) {
   if (a.w.K % 64 != 0 || a.w.bs != 64) return false;
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
   const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
-  return gemv_smem(wk, a.w.K, 32) <= 227 * 1024;
+  if (a.w.N > 0x7fffffff || a.w.K > 0x7fffffff || (a.w.N * a.w.K) / 2 > 0xfffffff0ll) return false;
+  return gemv_smem(wk, a.w.K, 32, a.M, a.r) <= 113 * 1024;
 }
 
 template <int DT, int WK, int MT>
 static int gemv_launch(const GemvArgs& g, size_t smem, cudaStream_t st) {
   auto kern = gemv_k<DT, WK, MT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) {
-    set_cuda_error(e);
-    return RQ_ERR_CUDA;
-  }
+  const int rc = ensure_smem_limit((const void*)kern, smem);
+  if (rc != RQ_OK) return rc;
   kern<<<g.grid, kGemvThreads, smem, st>>>(g);
   return check_launch();
 }
@@ -320,12 +365,13 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
   g.s = a.scaling;
   g.y = a.y;
   const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
-  g.chunk_rows = gemv_smem(wk, a.w.K, 64) <= 227 * 1024 ? 64 : 32;
+  // two CTAs per SM; each owns ~N / (2 * SMs) consecutive output rows
+  g.chunk_rows = gemv_smem(wk, a.w.K, 64, a.M, a.r) <= 113 * 1024 ? 64 : 32;
   const int64_t sms = num_sms();
-  int64_t grid = sms;
+  int64_t grid = 2 * sms;
   if (grid * 8 > a.w.N) grid = (a.w.N + 7) / 8;
   g.grid = (int)grid;
-  const size_t smem = gemv_smem(wk, a.w.K, g.chunk_rows);
+  const size_t smem = gemv_smem(wk, a.w.K, g.chunk_rows, a.M, a.r);
   return a.xdt == RQ_BF16 ? gemv_dt<RQ_BF16>(g, wk, smem, st) : gemv_dt<RQ_F16>(g, wk, smem, st);
 }
 

@@ -160,6 +160,135 @@ __global__ void __launch_bounds__(32 * WM) lora_down_mma_k(const typename DType<
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;  // leave the counter area zeroed
 }
 
+// Small M (<= 16): a cluster of kLoraCluster CTAs x 16 warps splits the
+// reduction dimension; each CTA reduces its warps in shared memory, then
+// every CTA sums its share of the outputs over the cluster's partials
+// through distributed shared memory, in rank order (deterministic).  A warp
+// issues the loads of KB k-steps before their MMAs.  NT = r/8 rounded up
+// to 2, 4 or 8 (r <= 64).
+constexpr int kLoraCluster = 8;
+constexpr int kLoraSmallMaxR = 64;
+constexpr int kLoraSmallWarps = 16;
+
+template <int DT, bool WT, int NT>
+__global__ void __cluster_dims__(kLoraCluster, 1, 1) __launch_bounds__(kLoraSmallWarps * 32)
+    lora_down_small_k(const typename DType<DT>::T* __restrict__ X, int M, int Kr,
+                      const typename DType<DT>::T* __restrict__ W2, int R, float pre_s, int do_pre,
+                      typename DType<DT>::T* __restrict__ out) {
+  using T = typename DType<DT>::T;
+  constexpr int RP = NT * 8;            // padded output columns
+  constexpr int KB = NT <= 4 ? 8 : 4;   // k-steps per load batch
+  extern __shared__ float lsm[];
+  float* part = lsm;                              // [warps][16][RP]
+  float* cta = lsm + kLoraSmallWarps * 16 * RP;   // [16][RP]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const unsigned rank = blockIdx.x % kLoraCluster;
+  const int ksteps = (Kr + 15) / 16;
+  const int nw = kLoraSmallWarps * kLoraCluster;
+  const int gw = rank * kLoraSmallWarps + warp;
+  const int s0 = ksteps * gw / nw, s1 = ksteps * (gw + 1) / nw;
+  const bool vec_x = ((uintptr_t)X % 4 == 0) && (Kr % 2 == 0);
+  const bool vec_w = ((uintptr_t)W2 % 4 == 0) && (Kr % 2 == 0);
+  float acc[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+  const T* xa = X + (size_t)(g < M ? g : 0) * Kr;
+  const T* xb = X + (size_t)(g + 8 < M ? g + 8 : 0) * Kr;
+  for (int sb = s0; sb < s1; sb += KB) {
+    uint32_t a[KB][4];
+    uint32_t bw[KB][NT][2];
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+      const int k0 = (sb + q) * 16;
+      const bool on = sb + q < s1;
+      a[q][0] = on && g < M ? ld_pair<DT>(xa, k0 + 2 * t, Kr, vec_x) : 0u;
+      a[q][1] = on && g + 8 < M ? ld_pair<DT>(xb, k0 + 2 * t, Kr, vec_x) : 0u;
+      a[q][2] = on && g < M ? ld_pair<DT>(xa, k0 + 8 + 2 * t, Kr, vec_x) : 0u;
+      a[q][3] = on && g + 8 < M ? ld_pair<DT>(xb, k0 + 8 + 2 * t, Kr, vec_x) : 0u;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int n = nt * 8 + g;
+        uint32_t b0 = 0, b1 = 0;
+        if (on && n < R) {
+          if (!WT) {
+            b0 = ld_pair<DT>(W2 + (size_t)n * Kr, k0 + 2 * t, Kr, vec_w);
+            b1 = ld_pair<DT>(W2 + (size_t)n * Kr, k0 + 8 + 2 * t, Kr, vec_w);
+          } else {
+            const int ka = k0 + 2 * t, kb = k0 + 8 + 2 * t;
+            const uint32_t e0 = ka < Kr ? bits16<DT>(W2[(size_t)ka * R + n]) : 0u;
+            const uint32_t e1 = ka + 1 < Kr ? bits16<DT>(W2[(size_t)(ka + 1) * R + n]) : 0u;
+            const uint32_t e2 = kb < Kr ? bits16<DT>(W2[(size_t)kb * R + n]) : 0u;
+            const uint32_t e3 = kb + 1 < Kr ? bits16<DT>(W2[(size_t)(kb + 1) * R + n]) : 0u;
+            b0 = e0 | (e1 << 16);
+            b1 = e2 | (e3 << 16);
+          }
+        }
+        bw[q][nt][0] = b0;
+        bw[q][nt][1] = b1;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+      if (do_pre) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[q][i] = prescale_pair<DT>(a[q][i], pre_s);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) MmaOp<DT>::mma(acc[nt], a[q], bw[q][nt][0], bw[q][nt][1]);
+    }
+  }
+  float* mine = part + warp * 16 * RP;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int c = nt * 8 + 2 * t;
+    mine[g * RP + c] = acc[nt][0];
+    mine[g * RP + c + 1] = acc[nt][1];
+    mine[(g + 8) * RP + c] = acc[nt][2];
+    mine[(g + 8) * RP + c + 1] = acc[nt][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * RP; i += blockDim.x) {
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kLoraSmallWarps; ++w) v += part[w * 16 * RP + i];
+    cta[i] = v;
+  }
+  // every CTA of the cluster has its partial in shared memory
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+  const int total = M * R;
+  const int share = (total + kLoraCluster - 1) / kLoraCluster;
+  const uint32_t cta_addr = (uint32_t)__cvta_generic_to_shared(cta);
+  for (int o = rank * share + threadIdx.x; o < total && o < (int)(rank + 1) * share; o += blockDim.x) {
+    const int m = o / R, c = o % R;
+    const uint32_t off = (uint32_t)(m * RP + c) * 4;
+    float sum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kLoraCluster; ++q) {
+      uint32_t remote;
+      float v;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(cta_addr + off), "r"(q));
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+      sum += v;
+    }
+    out[(size_t)m * R + c] = DType<DT>::from_f32(sum);
+  }
+  // keep this CTA's shared memory alive until the cluster has read it
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+template <int DT, bool WT, int NT>
+static int lora_small_launch(const void* X, int M, int Kr, const void* W2, int R, float pre_s, int do_pre, void* out,
+                             cudaStream_t st) {
+  using T = typename DType<DT>::T;
+  const size_t smem = (size_t)(kLoraSmallWarps + 1) * 16 * NT * 8 * sizeof(float);
+  auto kern = lora_down_small_k<DT, WT, NT>;
+  const int rc = ensure_smem_limit((const void*)kern, smem);
+  if (rc != RQ_OK) return rc;
+  kern<<<kLoraCluster, kLoraSmallWarps * 32, smem, st>>>((const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre,
+                                                         (T*)out);
+  return check_launch();
+}
+
 // fp32 activations: one thread per output, CUDA cores.
 template <bool WT>
 __global__ void __launch_bounds__(256) lora_down_f32_k(const float* __restrict__ X, int64_t M, int64_t Kr,
@@ -183,6 +312,11 @@ static int lora_down_t(const void* X, int64_t M, int64_t Kr, const void* W2, int
                        void* out, float* partial, int64_t partial_elems, unsigned* counters, int ncounters,
                        cudaStream_t st) {
   using T = typename DType<DT>::T;
+  if (M <= 16 && R <= kLoraSmallMaxR && Kr <= 0x7fffffff) {
+    if (R <= 16) return lora_small_launch<DT, WT, 2>(X, (int)M, (int)Kr, W2, R, pre_s, do_pre, out, st);
+    if (R <= 32) return lora_small_launch<DT, WT, 4>(X, (int)M, (int)Kr, W2, R, pre_s, do_pre, out, st);
+    return lora_small_launch<DT, WT, 8>(X, (int)M, (int)Kr, W2, R, pre_s, do_pre, out, st);
+  }
   if (M <= 16) {
     // split the reduction so that ~128 single-warp CTAs share it
     int64_t ksplit = Kr / 256;

@@ -12,6 +12,10 @@ namespace rq {
 // Records the CUDA error of the last failing launch in this thread.
 void set_cuda_error(cudaError_t e);
 
+// Raises a kernel's dynamic shared memory limit to `bytes` on the current
+// device (once per kernel, device and size; thread-safe).
+int ensure_smem_limit(const void* kernel, size_t bytes);
+
 // Maps the launch status of the kernel just issued to an RQ_* status.
 inline int check_launch() {
   cudaError_t e = cudaGetLastError();
