@@ -53,7 +53,7 @@ template <> struct Mma16816<RQ_F16> {
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kGemvNT = 8;        // n-tiles of 8 rows held per warp (64 rows)
+constexpr int kGemvMaxNT = 8;     // 8-row tiles held per warp at most (64 rows)
 constexpr int kGemvStageU = 16;   // scale loads issued per thread before use
 
 struct GemvArgs {
@@ -67,36 +67,63 @@ struct GemvArgs {
   int r;
   float s;
   void* y;
-  int chunk_rows;      // 64 or 32
   int grid;
+  int tiles;           // ceil(N / 8)
+  int chunks;          // row chunks per CTA
 };
 
-// Shared-memory table entry of code byte v for lane `lane`: the two levels
-// of the byte (low nibble = even k) as a packed 16-bit pair.  32 copies, one
-// per bank, so a warp's 32 lookups never conflict.
-__device__ __forceinline__ uint32_t lut_get(uint32_t lut_lane_base, uint32_t v) {
+// mma.sync m16n8k16 with a zero accumulator input (starts a block partial)
+template <int DT> struct Mma16816Zero;
+template <> struct Mma16816Zero<RQ_BF16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+  }
+};
+template <> struct Mma16816Zero<RQ_F16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+  }
+};
+
+// Table entry of the code byte found at bit SH of `word`, for this lane.
+// The table holds 32 copies interleaved per byte value (entry v, copy l at
+// word v*32 + l), so lane l reads bank l: the address is lane_base + v*128,
+// one byte extract (prmt) and one shift-add (lea).
+template <int SH>
+__device__ __forceinline__ uint32_t lut_at(uint32_t word, uint32_t lane_base) {
+  const uint32_t v = __byte_perm(word, 0u, 0x4440u | (SH / 8));
   uint32_t r;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(lut_lane_base + (v << 7)));
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(lane_base + (v << 7)));
   return r;
 }
 
 // WK: 0 = NF4 family (table lookup, per-block scale), 1 = INT8 blockwise,
-//     2 = INT8 per-row.  MT: 8 (M <= 8) or 16.
-template <int DT, int WK, int MT>
+//     2 = INT8 per-row.  MT: 8 (M <= 8) or 16.  NT: 8-row tiles per chunk.
+template <int DT, int WK, int MT, int NT>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
   using T = typename DType<DT>::T;
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
   const int nbk = K / 64;
-  const int CH = p.chunk_rows;
-  const int SCS = CH + 2;  // scale-table row stride (floats)
+  constexpr int CH = NT * 8;
+  constexpr int SCS = CH + 2;  // scale-table row stride (floats)
 
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
   float* sc = reinterpret_cast<float*>(smem + (WK == 0 ? 256 * 32 * 4 : 0));
   float4* red = reinterpret_cast<float4*>(reinterpret_cast<unsigned char*>(sc) +
                                           (WK != 2 ? ((nbk * SCS * 4 + 15) / 16) * 16 : 0));
-  T* tl = reinterpret_cast<T*>(red + kGemvWarps * kGemvNT * 32);  // staged x.A^T [M, r]
+  T* tl = reinterpret_cast<T*>(red + kGemvWarps * NT * 32);  // staged x.A^T [M, r]
 
   if constexpr (WK == 0) {
     for (int i = tid; i < 256 * 32; i += kGemvThreads) {
@@ -108,33 +135,36 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
     const T* td = static_cast<const T*>(p.tdown);
     for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
   }
-  const uint32_t lut_lane = (uint32_t)__cvta_generic_to_shared(lut) + lane * 4;
+  const uint32_t lane4 = (uint32_t)__cvta_generic_to_shared(lut) + lane * 4;
 
-  const int r_begin = (int)((int64_t)N * blockIdx.x / p.grid);
-  const int r_end = (int)((int64_t)N * (blockIdx.x + 1) / p.grid);
+  const int tile_begin = (int)((int64_t)p.tiles * blockIdx.x / p.grid);
+  const int tile_end = (int)((int64_t)p.tiles * (blockIdx.x + 1) / p.grid);
   const int kb0 = nbk * warp / kGemvWarps, kb1 = nbk * (warp + 1) / kGemvWarps;
   const uint8_t* qb = static_cast<const uint8_t*>(p.w.q);
   const T* xp = static_cast<const T*>(p.x);
   const bool rowa = g < M, rowb = (MT == 16) && (g + 8 < M);
   const T* xa = xp + (size_t)(rowa ? g : 0) * K + t * 16;
   const T* xb = xp + (size_t)(rowb ? g + 8 : 0) * K + t * 16;
-  constexpr int CW = (WK == 0) ? 2 : 4;   // 32-bit words of codes per lane per n-tile per block
+  constexpr int CW = (WK == 0) ? 2 : 4;   // 32-bit words of codes per lane per tile per block
   constexpr int RB = (WK == 0) ? 32 : 64; // code bytes per row per block
 
-  for (int c0 = r_begin; c0 < r_end; c0 += CH) {
-    const int R = r_end - c0 < CH ? r_end - c0 : CH;
-    const int ntiles = (R + 7) >> 3;
-    // per-lane byte offsets of this lane's weight row in each n-tile
-    uint32_t roff[kGemvNT];
+  const int ntot = tile_end - tile_begin;
+  for (int ch = 0; ch < p.chunks; ++ch) {
+    const int t0 = tile_begin + (int)((int64_t)ntot * ch / p.chunks);
+    const int t1 = tile_begin + (int)((int64_t)ntot * (ch + 1) / p.chunks);
+    const int ntiles = t1 - t0;
+    const int c0 = t0 * 8;
+    const int R = (t1 * 8 < N ? t1 * 8 : N) - c0;
+    if (R <= 0) break;
+    uint32_t roff[NT];
 #pragma unroll
-    for (int nt = 0; nt < kGemvNT; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
       const int rl = nt * 8 + g;
-      roff[nt] = rl < R ? (uint32_t)((c0 + rl) * (uint32_t)(K / 64) * RB) + t * (RB / 4) : 0xFFFFFFFFu;
+      roff[nt] = rl < R ? (uint32_t)(c0 + rl) * (uint32_t)(nbk * RB) + t * (RB / 4) : 0xFFFFFFFFu;
     }
-    uint32_t cur[kGemvNT][CW];
-    auto load_codes = [&](int b, uint32_t (&dst)[kGemvNT][CW]) {
+    auto load_codes = [&](int b, uint32_t (&dst)[NT][CW]) {
 #pragma unroll
-      for (int nt = 0; nt < kGemvNT; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
         if (nt < ntiles && roff[nt] != 0xFFFFFFFFu) {
           const unsigned char* src = qb + roff[nt] + (uint32_t)b * RB;
           if constexpr (WK == 0) {
@@ -150,7 +180,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
         }
       }
     };
-    uint32_t xc[16];
     auto load_x = [&](int b, uint32_t (&dst)[16]) {
       if (rowa) {
         const uint4* s = reinterpret_cast<const uint4*>(xa + b * 64);
@@ -171,14 +200,58 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
         for (int i = 8; i < 16; ++i) dst[i] = 0u;
       }
     };
-    // first block's operands go out before the scale staging so their
-    // latency overlaps it
-    // NF4 prefetches one block ahead; INT8 (twice the code bytes, and the
-    // registers to match) loads each block in place
-    constexpr bool kPrefetchCodes = (WK == 0);
+
+    float acc[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+
+    // one block of MMAs for all tiles from (codes, x) register sets
+    auto block_mma = [&](int b, const uint32_t (&cd)[NT][CW], const uint32_t (&xc)[16]) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (nt < ntiles) {
+          float part[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t b0, b1;
+            if constexpr (WK == 0) {
+              const uint32_t word = cd[nt][j >> 1];
+              if (j & 1) {
+                b0 = lut_at<16>(word, lane4);
+                b1 = lut_at<24>(word, lane4);
+              } else {
+                b0 = lut_at<0>(word, lane4);
+                b1 = lut_at<8>(word, lane4);
+              }
+            } else {
+              const uint32_t word = cd[nt][j];
+              b0 = pack2<DT>((float)(int8_t)(word & 0xFF), (float)(int8_t)((word >> 8) & 0xFF));
+              b1 = pack2<DT>((float)(int8_t)((word >> 16) & 0xFF), (float)(int8_t)(word >> 24));
+            }
+            if constexpr (WK == 2)
+              Mma16816<DT>::run(acc[nt], xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
+            else if (j == 0)
+              Mma16816Zero<DT>::run(part, xc[0], xc[8], xc[1], xc[9], b0, b1);
+            else
+              Mma16816<DT>::run(part, xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
+          }
+          if constexpr (WK != 2) {
+            const float2 s2 = *reinterpret_cast<const float2*>(&sc[b * SCS + nt * 8 + 2 * t]);
+            acc[nt][0] = fmaf(part[0], s2.x, acc[nt][0]);
+            acc[nt][1] = fmaf(part[1], s2.y, acc[nt][1]);
+            acc[nt][2] = fmaf(part[2], s2.x, acc[nt][2]);
+            acc[nt][3] = fmaf(part[3], s2.y, acc[nt][3]);
+          }
+        }
+      }
+    };
+
+    // NF4 keeps two blocks of codes in flight (ping-pong); INT8 (twice the
+    // code bytes) loads each block where it is used.
+    uint32_t cA[NT][CW], cB[NT][CW], xA[16], xB[16];
     if (kb0 < kb1) {
-      if (kPrefetchCodes) load_codes(kb0, cur);
-      load_x(kb0, xc);
+      if constexpr (WK == 0) load_codes(kb0, cA);
+      load_x(kb0, xA);
     }
     if constexpr (WK != 2) {
       // scales of rows c0..c0+R-1: a contiguous run of R*nbk blocks; all
@@ -201,73 +274,30 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
           }
         }
       }
-      for (int idx = tid; idx < (CH - R) * nbk; idx += kGemvThreads) {
-        const int rl = R + idx / nbk, b = idx % nbk;
-        sc[b * SCS + rl] = 0.0f;
-      }
     }
     __syncthreads();
 
-    float acc[kGemvNT][4];
-#pragma unroll
-    for (int i = 0; i < kGemvNT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-
-    for (int b = kb0; b < kb1; ++b) {
-      uint32_t nxt[kGemvNT][CW];
-      uint32_t xn[16];
-      const bool more = b + 1 < kb1;
-      if (more) {
-        if (kPrefetchCodes) load_codes(b + 1, nxt);
-        load_x(b + 1, xn);
+    for (int b = kb0; b < kb1; b += 2) {
+      const bool has2 = b + 1 < kb1;
+      if (has2) {
+        if constexpr (WK == 0) load_codes(b + 1, cB);
+        load_x(b + 1, xB);
       }
-      if (!kPrefetchCodes) load_codes(b, cur);
-#pragma unroll
-      for (int nt = 0; nt < kGemvNT; ++nt) {
-        if (nt < ntiles) {
-          float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t b0, b1;
-            if constexpr (WK == 0) {
-              const uint32_t word = cur[nt][j >> 1];
-              const int sh = 16 * (j & 1);
-              b0 = lut_get(lut_lane, (word >> sh) & 0xFFu);
-              b1 = lut_get(lut_lane, (word >> (sh + 8)) & 0xFFu);
-            } else {
-              const uint32_t word = cur[nt][j];
-              b0 = pack2<DT>((float)(int8_t)(word & 0xFF), (float)(int8_t)((word >> 8) & 0xFF));
-              b1 = pack2<DT>((float)(int8_t)((word >> 16) & 0xFF), (float)(int8_t)(word >> 24));
-            }
-            if constexpr (WK == 2)
-              Mma16816<DT>::run(acc[nt], xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
-            else
-              Mma16816<DT>::run(part, xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
-          }
-          if constexpr (WK != 2) {
-            const float2 s2 = *reinterpret_cast<const float2*>(&sc[b * SCS + nt * 8 + 2 * t]);
-            acc[nt][0] = fmaf(part[0], s2.x, acc[nt][0]);
-            acc[nt][1] = fmaf(part[1], s2.y, acc[nt][1]);
-            acc[nt][2] = fmaf(part[2], s2.x, acc[nt][2]);
-            acc[nt][3] = fmaf(part[3], s2.y, acc[nt][3]);
-          }
-        }
+      if constexpr (WK != 0) load_codes(b, cA);
+      block_mma(b, cA, xA);
+      if (!has2) break;
+      if (b + 2 < kb1) {
+        if constexpr (WK == 0) load_codes(b + 2, cA);
+        load_x(b + 2, xA);
       }
-      if (more) {
-        if (kPrefetchCodes) {
-#pragma unroll
-          for (int nt = 0; nt < kGemvNT; ++nt)
-#pragma unroll
-            for (int i = 0; i < CW; ++i) cur[nt][i] = nxt[nt][i];
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) xc[i] = xn[i];
-      }
+      if constexpr (WK != 0) load_codes(b + 1, cB);
+      block_mma(b + 1, cB, xB);
     }
 
 #pragma unroll
-    for (int nt = 0; nt < kGemvNT; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
       if (nt < ntiles)
-        red[(warp * kGemvNT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+        red[(warp * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
     __syncthreads();
 
     const bool has_bias = p.bias != nullptr, has_lora = p.r > 0;
@@ -281,7 +311,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
       float sum = 0.0f;
 #pragma unroll
       for (int w = 0; w < kGemvWarps; ++w) {
-        const float* rv = reinterpret_cast<const float*>(&red[(w * kGemvNT + nt) * 32 + ln]);
+        const float* rv = reinterpret_cast<const float*>(&red[(w * NT + nt) * 32 + ln]);
         sum += rv[comp];
       }
       const int row = c0 + nl;
@@ -313,14 +343,36 @@ static int num_sms() {
   return cached[dev];
 }
 
-// Shared memory the GEMV needs for this K, chunk height and adapter size.
-static size_t gemv_smem(int wk, int64_t K, int chunk, int64_t M, int r) {
+// Shared memory the GEMV needs for this K, tile count and adapter size.
+static size_t gemv_smem(int wk, int64_t K, int nt, int64_t M, int r) {
   size_t s = 0;
   if (wk == 0) s += 256 * 32 * 4;
-  if (wk != 2) s += ((size_t)(K / 64) * (chunk + 2) * 4 + 15) / 16 * 16;
-  s += (size_t)kGemvWarps * kGemvNT * 32 * 16;
+  if (wk != 2) s += ((size_t)(K / 64) * (nt * 8 + 2) * 4 + 15) / 16 * 16;
+  s += (size_t)kGemvWarps * nt * 32 * 16;
   s += (size_t)M * r * 2;
   return s;
+}
+
+constexpr size_t kGemvSmemCap = 113 * 1024;  // two CTAs per SM
+
+// Launch shape: two CTAs per SM, each owning ceil(N/8)/grid whole 8-row
+// tiles, processed in `chunks` passes of at most NT <= 8 tiles.
+static void gemv_shape(int wk, int64_t N, int64_t K, int64_t M, int r, int* grid, int* tiles, int* chunks,
+                       int* nt) {
+  const int64_t T = (N + 7) / 8;
+  int64_t G = 2 * num_sms();
+  if (G > T) G = T;
+  const int64_t per = (T + G - 1) / G;
+  int64_t ch = (per + kGemvMaxNT - 1) / kGemvMaxNT;
+  int64_t n = (per + ch - 1) / ch;
+  while (n > 1 && gemv_smem(wk, K, (int)n, M, r) > kGemvSmemCap) {
+    ++ch;
+    n = (per + ch - 1) / ch;
+  }
+  *grid = (int)G;
+  *tiles = (int)T;
+  *chunks = (int)ch;
+  *nt = (int)n;
 }
 
 bool gemv_supported(const LinearArgs& a) {
@@ -328,27 +380,45 @@ bool gemv_supported(const LinearArgs& a) {
   if (a.xdt != RQ_BF16 && a.xdt != RQ_F16) return false;
   if (a.w.K % 64 != 0 || a.w.bs != 64) return false;
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
-  const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
   if (a.w.N > 0x7fffffff || a.w.K > 0x7fffffff || (a.w.N * a.w.K) / 2 > 0xfffffff0ll) return false;
-  return gemv_smem(wk, a.w.K, 32, a.M, a.r) <= 113 * 1024;
+  const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
+  return gemv_smem(wk, a.w.K, 1, a.M, a.r) <= kGemvSmemCap;
 }
 
-template <int DT, int WK, int MT>
+template <int DT, int WK, int MT, int NT>
 static int gemv_launch(const GemvArgs& g, size_t smem, cudaStream_t st) {
-  auto kern = gemv_k<DT, WK, MT>;
+  auto kern = gemv_k<DT, WK, MT, NT>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
   kern<<<g.grid, kGemvThreads, smem, st>>>(g);
   return check_launch();
 }
 
+template <int DT, int WK, int MT>
+static int gemv_nt(const GemvArgs& g, int nt, size_t smem, cudaStream_t st) {
+  if constexpr (WK == 0) {
+    switch (nt) {
+      case 1: return gemv_launch<DT, WK, MT, 1>(g, smem, st);
+      case 2: return gemv_launch<DT, WK, MT, 2>(g, smem, st);
+      case 3: return gemv_launch<DT, WK, MT, 3>(g, smem, st);
+      case 4: return gemv_launch<DT, WK, MT, 4>(g, smem, st);
+      case 5: return gemv_launch<DT, WK, MT, 5>(g, smem, st);
+      case 6: return gemv_launch<DT, WK, MT, 6>(g, smem, st);
+      case 7: return gemv_launch<DT, WK, MT, 7>(g, smem, st);
+      default: return gemv_launch<DT, WK, MT, 8>(g, smem, st);
+    }
+  } else {
+    return nt <= 4 ? gemv_launch<DT, WK, MT, 4>(g, smem, st) : gemv_launch<DT, WK, MT, 8>(g, smem, st);
+  }
+}
+
 template <int DT>
-static int gemv_dt(const GemvArgs& g, int wk, size_t smem, cudaStream_t st) {
+static int gemv_dt(const GemvArgs& g, int wk, int nt, size_t smem, cudaStream_t st) {
   const bool m16 = g.M > 8;
   switch (wk) {
-    case 0: return m16 ? gemv_launch<DT, 0, 16>(g, smem, st) : gemv_launch<DT, 0, 8>(g, smem, st);
-    case 1: return m16 ? gemv_launch<DT, 1, 16>(g, smem, st) : gemv_launch<DT, 1, 8>(g, smem, st);
-    default: return m16 ? gemv_launch<DT, 2, 16>(g, smem, st) : gemv_launch<DT, 2, 8>(g, smem, st);
+    case 0: return m16 ? gemv_nt<DT, 0, 16>(g, nt, smem, st) : gemv_nt<DT, 0, 8>(g, nt, smem, st);
+    case 1: return m16 ? gemv_nt<DT, 1, 16>(g, nt, smem, st) : gemv_nt<DT, 1, 8>(g, nt, smem, st);
+    default: return m16 ? gemv_nt<DT, 2, 16>(g, nt, smem, st) : gemv_nt<DT, 2, 8>(g, nt, smem, st);
   }
 }
 
@@ -365,14 +435,14 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
   g.s = a.scaling;
   g.y = a.y;
   const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
-  // two CTAs per SM; each owns ~N / (2 * SMs) consecutive output rows
-  g.chunk_rows = gemv_smem(wk, a.w.K, 64, a.M, a.r) <= 113 * 1024 ? 64 : 32;
-  const int64_t sms = num_sms();
-  int64_t grid = 2 * sms;
-  if (grid * 8 > a.w.N) grid = (a.w.N + 7) / 8;
-  g.grid = (int)grid;
-  const size_t smem = gemv_smem(wk, a.w.K, g.chunk_rows, a.M, a.r);
-  return a.xdt == RQ_BF16 ? gemv_dt<RQ_BF16>(g, wk, smem, st) : gemv_dt<RQ_F16>(g, wk, smem, st);
+  int nt = 1;
+  gemv_shape(wk, a.w.N, a.w.K, a.M, a.r, &g.grid, &g.tiles, &g.chunks, &nt);
+  if (wk != 0) {
+    nt = nt <= 4 ? 4 : 8;
+    g.chunks = (int)(((g.tiles + g.grid - 1) / g.grid + nt - 1) / nt);
+  }
+  const size_t smem = gemv_smem(wk, a.w.K, nt, a.M, a.r);
+  return a.xdt == RQ_BF16 ? gemv_dt<RQ_BF16>(g, wk, nt, smem, st) : gemv_dt<RQ_F16>(g, wk, nt, smem, st);
 }
 
 }  // namespace rq
