@@ -33,7 +33,7 @@ template <int DT> struct Mma16816;
 template <> struct Mma16816<RQ_BF16> {
   static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -43,7 +43,7 @@ template <> struct Mma16816<RQ_BF16> {
 template <> struct Mma16816<RQ_F16> {
   static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -77,7 +77,7 @@ template <int DT> struct Mma16816Zero;
 template <> struct Mma16816Zero<RQ_BF16> {
   static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%10,%10,%10};\n"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -87,7 +87,7 @@ template <> struct Mma16816Zero<RQ_BF16> {
 template <> struct Mma16816Zero<RQ_F16> {
   static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%10,%10,%10};\n"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -97,14 +97,12 @@ template <> struct Mma16816Zero<RQ_F16> {
 
 // Table entry of the code byte found at bit SH of `word`, for this lane.
 // The table holds 32 copies interleaved per byte value (entry v, copy l at
-// word v*32 + l), so lane l reads bank l: the address is lane_base + v*128,
-// one byte extract (prmt) and one shift-add (lea).
+// word v*32 + l), so lane l reads bank l: one byte extract (prmt) and one
+// indexed shared load.
 template <int SH>
-__device__ __forceinline__ uint32_t lut_at(uint32_t word, uint32_t lane_base) {
+__device__ __forceinline__ uint32_t lut_at(uint32_t word, const uint32_t* lut_lane) {
   const uint32_t v = __byte_perm(word, 0u, 0x4440u | (SH / 8));
-  uint32_t r;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(lane_base + (v << 7)));
-  return r;
+  return lut_lane[v << 5];
 }
 
 // WK: 0 = NF4 family (table lookup, per-block scale), 1 = INT8 blockwise,
@@ -135,7 +133,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
     const T* td = static_cast<const T*>(p.tdown);
     for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
   }
-  const uint32_t lane4 = (uint32_t)__cvta_generic_to_shared(lut) + lane * 4;
+  const uint32_t* lane4 = lut + lane;
 
   const int tile_begin = (int)((int64_t)p.tiles * blockIdx.x / p.grid);
   const int tile_end = (int)((int64_t)p.tiles * (blockIdx.x + 1) / p.grid);
@@ -254,28 +252,29 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
       load_x(kb0, xA);
     }
     if constexpr (WK != 2) {
-      // scales of rows c0..c0+R-1: a contiguous run of R*nbk blocks; all
-      // loads of a round are issued before any is used
-      const int total = R * nbk;
-      const int64_t gbase = (int64_t)c0 * nbk;
-      for (int base = tid; base < total; base += kGemvThreads * kGemvStageU) {
+      // each warp expands the scales of its own blocks for all rows of the
+      // chunk (no CTA barrier needed); all loads of a round are issued
+      // before any is used
+      const int nbw = kb1 - kb0;
+      const int total = R * nbw;
+      const float inv = 1.0f / (float)(nbw > 0 ? nbw : 1);
+      for (int base = lane; base < total; base += 32 * kGemvStageU) {
         float v[kGemvStageU];
+        int rl[kGemvStageU], bb[kGemvStageU];
 #pragma unroll
         for (int u = 0; u < kGemvStageU; ++u) {
-          const int idx = base + u * kGemvThreads;
-          v[u] = idx < total ? block_scale(p.w, gbase + idx) : 0.0f;
+          const int idx = base + u * 32;
+          rl[u] = __float2int_rz(((float)idx + 0.5f) * inv);
+          bb[u] = idx - rl[u] * nbw;
+          v[u] = idx < total ? block_scale(p.w, (int64_t)(c0 + rl[u]) * nbk + kb0 + bb[u]) : 0.0f;
         }
 #pragma unroll
-        for (int u = 0; u < kGemvStageU; ++u) {
-          const int idx = base + u * kGemvThreads;
-          if (idx < total) {
-            const int rl = idx / nbk, b = idx - rl * nbk;
-            sc[b * SCS + rl] = v[u];
-          }
-        }
+        for (int u = 0; u < kGemvStageU; ++u)
+          if (base + u * 32 < total) sc[(kb0 + bb[u]) * SCS + rl[u]] = v[u];
       }
+      __syncwarp();
     }
-    __syncthreads();
+    if (ch == 0) __syncthreads();  // the code table is complete
 
     for (int b = kb0; b < kb1; b += 2) {
       const bool has2 = b + 1 < kb1;
