@@ -44,6 +44,7 @@ extern "C" {
 #define RQ_ERR_CUDA (-4)        /* CUDA launch or runtime error */
 #define RQ_ERR_WORKSPACE (-5)   /* workspace missing or too small */
 #define RQ_ERR_DEVICE (-6)      /* current device is not sm_100 */
+#define RQ_ERR_SCRATCH (-7)     /* needs more than rq_linear_forward_noalloc's built-in scratch */
 
 #define RQ_F32 0
 #define RQ_BF16 1
@@ -148,6 +149,29 @@ RQ_API int rq_linear_dx(int wfmt, const void* qweight, const void* scales, int s
                  const void* dy, int xdtype, int64_t M,
                  const void* lora_a, const void* lora_b, int r, float scaling,
                  void* dx, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Bytes of device scratch compiled into the library for
+ * rq_linear_forward_noalloc (held on every GPU that loads the library). */
+#define RQ_NOALLOC_SCRATCH_BYTES (2u << 20)
+
+/* rq_linear_forward for callers that cannot allocate device memory (plugin
+ * hosts that own all device memory and hand out no workspace, cgo / JNI /
+ * FFI bindings without a CUDA allocator, loops where cudaMalloc would
+ * synchronize the device).  Same arguments and result as rq_linear_forward
+ * minus the workspace: the scratch is a fixed RQ_NOALLOC_SCRATCH_BYTES
+ * device array inside the library, so nothing is allocated.  Calls whose
+ * rq_linear_workspace_bytes(M, N, K, r) exceeds that size return
+ * RQ_ERR_SCRATCH before touching the GPU.  The first call on a device looks
+ * up the array's device address (make it before any stream capture).  All
+ * calls share the array: calls that may overlap on the GPU race and must not
+ * be issued.  This entry point has no counterpart in the reference. */
+RQ_API int rq_linear_forward_noalloc(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                      const uint8_t* c2, const float* c2_scales,
+                      int64_t N, int64_t K, int block_size,
+                      const void* x, int xdtype, int64_t M, const void* lora_x,
+                      const void* bias, int bias_dtype,
+                      const void* lora_a, const void* lora_b, int r, float scaling,
+                      void* y, void* stream);
 
 /* ------------------------------------- reference launcher drop-ins */
 

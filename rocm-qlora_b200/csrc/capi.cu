@@ -126,6 +126,7 @@ const char* rq_status_string(int s) {
     case RQ_ERR_CUDA: return "CUDA error";
     case RQ_ERR_WORKSPACE: return "workspace missing or too small";
     case RQ_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case RQ_ERR_SCRATCH: return "request exceeds the built-in scratch of rq_linear_forward_noalloc";
   }
   return "unknown status";
 }

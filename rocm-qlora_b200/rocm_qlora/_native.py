@@ -58,6 +58,7 @@ def _bind(L: ctypes.CDLL) -> None:
         "rq_linear_workspace_bytes": ([I64, I64, I64, I], I64),
         "rq_linear_forward": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, P, I, P, P, I, F, P, P, I64, P], I),
         "rq_linear_dx": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, P, I, F, P, P, I64, P], I),
+        "rq_linear_forward_noalloc": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, P, I, P, P, I, F, P, P], I),
         "launch_int4_dequant_matmul": ([P, P, P, P, P, I, I, I, I], None),
         "launch_int8_dequant_matmul": ([P, P, P, P, P, I, I, I, I], None),
     }
@@ -72,7 +73,7 @@ def exported_symbols() -> Tuple[str, ...]:
     return ("rq_abi_version", "rq_status_string", "rq_last_cuda_error", "rq_last_status",
             "rq_nf4_quantize", "rq_nf4_dequantize", "rq_int8_quantize", "rq_int8_quantize_rows",
             "rq_int8_dequantize", "rq_dq_quantize_scales", "rq_dq_dequantize",
-            "rq_linear_workspace_bytes", "rq_linear_forward", "rq_linear_dx",
+            "rq_linear_workspace_bytes", "rq_linear_forward", "rq_linear_dx", "rq_linear_forward_noalloc",
             "launch_int4_dequant_matmul", "launch_int8_dequant_matmul")
 
 
