@@ -60,6 +60,11 @@ extern "C" {
 RQ_API int rq_abi_version(void);                 /* bumps on any ABI change */
 RQ_API const char* rq_status_string(int status);
 RQ_API int rq_last_cuda_error(void);             /* cudaError_t of the last RQ_ERR_CUDA in this thread */
+/* Number of bounded in-kernel waits that ran out on the current device since
+ * the last call (and reset it).  Nonzero means a kernel stopped early and its
+ * output is not valid; it indicates a bug, never a normal condition.
+ * Synchronous. */
+RQ_API int rq_take_kernel_timeouts(unsigned int* count);
 
 /* -------------------------------------------------------- quantization */
 

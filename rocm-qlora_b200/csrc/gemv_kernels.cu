@@ -25,85 +25,11 @@
 // the output stays within the parity tolerance (tests/tolerance.py).
 #include <cuda_runtime.h>
 
-#include "linear_common.cuh"
+#include "gemv_common.cuh"
 
 namespace rq {
 
-template <int DT> struct Mma16816;
-template <> struct Mma16816<RQ_BF16> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
-    asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-};
-template <> struct Mma16816<RQ_F16> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
-    asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-};
-
-constexpr int kGemvWarps = 8;
-constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kGemvMaxNT = 8;     // 8-row tiles held per warp at most (64 rows)
-constexpr int kGemvStageU = 16;   // scale loads issued per thread before use
-
-struct GemvArgs {
-  QWeight w;
-  const void* x;
-  int64_t M;
-  const void* bias;
-  int bdt;
-  const void* tdown;   // [M, r] rounded x.A^T, activation dtype
-  const void* lora_b;  // [N, r]
-  int r;
-  float s;
-  void* y;
-  int grid;
-  int tiles;           // ceil(N / 8)
-  int chunks;          // row chunks per CTA
-};
-
-// mma.sync m16n8k16 with a zero accumulator input (starts a block partial)
-template <int DT> struct Mma16816Zero;
-template <> struct Mma16816Zero<RQ_BF16> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
-    asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};\n"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
-  }
-};
-template <> struct Mma16816Zero<RQ_F16> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
-    asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};\n"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
-  }
-};
-
-// Table entry of the code byte found at bit SH of `word`, for this lane.
-// The table holds 32 copies interleaved per byte value (entry v, copy l at
-// word v*32 + l), so lane l reads bank l: one byte extract (prmt) and one
-// indexed shared load.
-template <int SH>
-__device__ __forceinline__ uint32_t lut_at(uint32_t word, const uint32_t* lut_lane) {
-  const uint32_t v = __byte_perm(word, 0u, 0x4440u | (SH / 8));
-  return lut_lane[v << 5];
-}
+constexpr int kGemvStageU = 16;  // scale loads issued per thread before use
 
 // WK: 0 = NF4 family (table lookup, per-block scale), 1 = INT8 blockwise,
 //     2 = INT8 per-row.  MT: 8 (M <= 8) or 16.  NT: 8-row tiles per chunk.
@@ -329,19 +255,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
   }
 }
 
-static int num_sms() {
-  static int cached[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = v > 0 ? v : 148;
-  }
-  return cached[dev];
-}
-
 // Shared memory the GEMV needs for this K, tile count and adapter size.
 static size_t gemv_smem(int wk, int64_t K, int nt, int64_t M, int r) {
   size_t s = 0;
@@ -352,7 +265,10 @@ static size_t gemv_smem(int wk, int64_t K, int nt, int64_t M, int r) {
   return s;
 }
 
-constexpr size_t kGemvSmemCap = 113 * 1024;  // two CTAs per SM
+
+static size_t smem_for(int wk, int64_t K, int nt, int64_t M, int r) {
+  return wk == 0 ? gemv_nf4_smem(nt, M, r) : gemv_smem(wk, K, nt, M, r);
+}
 
 // Launch shape: two CTAs per SM, each owning ceil(N/8)/grid whole 8-row
 // tiles, processed in `chunks` passes of at most NT <= 8 tiles.
@@ -364,7 +280,7 @@ static void gemv_shape(int wk, int64_t N, int64_t K, int64_t M, int r, int* grid
   const int64_t per = (T + G - 1) / G;
   int64_t ch = (per + kGemvMaxNT - 1) / kGemvMaxNT;
   int64_t n = (per + ch - 1) / ch;
-  while (n > 1 && gemv_smem(wk, K, (int)n, M, r) > kGemvSmemCap) {
+  while (n > 1 && smem_for(wk, K, (int)n, M, r) > kGemvSmemCap) {
     ++ch;
     n = (per + ch - 1) / ch;
   }
@@ -381,7 +297,7 @@ bool gemv_supported(const LinearArgs& a) {
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
   if (a.w.N > 0x7fffffff || a.w.K > 0x7fffffff || (a.w.N * a.w.K) / 2 > 0xfffffff0ll) return false;
   const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
-  return gemv_smem(wk, a.w.K, 1, a.M, a.r) <= kGemvSmemCap;
+  return smem_for(wk, a.w.K, 1, a.M, a.r) <= kGemvSmemCap;
 }
 
 template <int DT, int WK, int MT, int NT>
@@ -395,30 +311,14 @@ static int gemv_launch(const GemvArgs& g, size_t smem, cudaStream_t st) {
 
 template <int DT, int WK, int MT>
 static int gemv_nt(const GemvArgs& g, int nt, size_t smem, cudaStream_t st) {
-  if constexpr (WK == 0) {
-    switch (nt) {
-      case 1: return gemv_launch<DT, WK, MT, 1>(g, smem, st);
-      case 2: return gemv_launch<DT, WK, MT, 2>(g, smem, st);
-      case 3: return gemv_launch<DT, WK, MT, 3>(g, smem, st);
-      case 4: return gemv_launch<DT, WK, MT, 4>(g, smem, st);
-      case 5: return gemv_launch<DT, WK, MT, 5>(g, smem, st);
-      case 6: return gemv_launch<DT, WK, MT, 6>(g, smem, st);
-      case 7: return gemv_launch<DT, WK, MT, 7>(g, smem, st);
-      default: return gemv_launch<DT, WK, MT, 8>(g, smem, st);
-    }
-  } else {
-    return nt <= 4 ? gemv_launch<DT, WK, MT, 4>(g, smem, st) : gemv_launch<DT, WK, MT, 8>(g, smem, st);
-  }
+  return nt <= 4 ? gemv_launch<DT, WK, MT, 4>(g, smem, st) : gemv_launch<DT, WK, MT, 8>(g, smem, st);
 }
 
 template <int DT>
 static int gemv_dt(const GemvArgs& g, int wk, int nt, size_t smem, cudaStream_t st) {
   const bool m16 = g.M > 8;
-  switch (wk) {
-    case 0: return m16 ? gemv_nt<DT, 0, 16>(g, nt, smem, st) : gemv_nt<DT, 0, 8>(g, nt, smem, st);
-    case 1: return m16 ? gemv_nt<DT, 1, 16>(g, nt, smem, st) : gemv_nt<DT, 1, 8>(g, nt, smem, st);
-    default: return m16 ? gemv_nt<DT, 2, 16>(g, nt, smem, st) : gemv_nt<DT, 2, 8>(g, nt, smem, st);
-  }
+  if (wk == 1) return m16 ? gemv_nt<DT, 1, 16>(g, nt, smem, st) : gemv_nt<DT, 1, 8>(g, nt, smem, st);
+  return m16 ? gemv_nt<DT, 2, 16>(g, nt, smem, st) : gemv_nt<DT, 2, 8>(g, nt, smem, st);
 }
 
 int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
@@ -433,13 +333,13 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
   g.r = a.r;
   g.s = a.scaling;
   g.y = a.y;
+  g.xdt = a.xdt;
   const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
   int nt = 1;
   gemv_shape(wk, a.w.N, a.w.K, a.M, a.r, &g.grid, &g.tiles, &g.chunks, &nt);
-  if (wk != 0) {
-    nt = nt <= 4 ? 4 : 8;
-    g.chunks = (int)(((g.tiles + g.grid - 1) / g.grid + nt - 1) / nt);
-  }
+  if (wk == 0) return gemv_nf4_launch(g, nt, st);
+  nt = nt <= 4 ? 4 : 8;
+  g.chunks = (int)(((g.tiles + g.grid - 1) / g.grid + nt - 1) / nt);
   const size_t smem = gemv_smem(wk, a.w.K, nt, a.M, a.r);
   return a.xdt == RQ_BF16 ? gemv_dt<RQ_BF16>(g, wk, nt, smem, st) : gemv_dt<RQ_F16>(g, wk, nt, smem, st);
 }
