@@ -267,7 +267,7 @@ static size_t gemv_smem(int wk, int64_t K, int nt, int64_t M, int r) {
 
 
 static size_t smem_for(int wk, int64_t K, int nt, int64_t M, int r) {
-  return wk == 0 ? gemv_nf4_smem(nt, M, r) : gemv_smem(wk, K, nt, M, r);
+  return wk == 0 ? gemv_nf4_smem(nt, K, M, r) : gemv_smem(wk, K, nt, M, r);
 }
 
 // Launch shape: two CTAs per SM, each owning ceil(N/8)/grid whole 8-row

@@ -33,7 +33,8 @@
 
 namespace rq {
 
-constexpr int kNf4Stages = 4;
+constexpr int kNf4MaxStages = 16;
+constexpr size_t kNf4RingBudget = 72 * 1024;  // ring bytes per CTA (two CTAs per SM)
 constexpr int kStageBlocks = kGemvWarps;            // one 64-block per warp per stage
 constexpr int kRowBytes = kStageBlocks * 32;         // code bytes per row per stage
 constexpr int kRowStride = kRowBytes + 32;           // padded: conflict-free 8-byte reads
@@ -79,11 +80,23 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                : "memory");
 }
 
-size_t gemv_nf4_smem(int nt, int64_t M, int r) {
+// Ring slots for a tile count: as many stages as the budget holds (the whole
+// K range when it fits), at least 2.
+int gemv_nf4_stages(int nt, int64_t K) {
+  const int64_t nst = (K / 64 + kStageBlocks - 1) / kStageBlocks;
+  int64_t s = (int64_t)(kNf4RingBudget / ((size_t)nt * 8 * kRowStride));
+  if (s > kNf4MaxStages) s = kNf4MaxStages;
+  if (s > nst) s = nst;
+  if (s < 2) s = 2;
+  return (int)s;
+}
+
+size_t gemv_nf4_smem(int nt, int64_t K, int64_t M, int r) {
+  const int S = gemv_nf4_stages(nt, K);
   return 256 * 32 * 4                                   // code-byte table
-         + (size_t)kNf4Stages * nt * 8 * kRowStride     // ring (the reduction reuses it)
+         + (size_t)S * nt * 8 * kRowStride              // ring (the reduction reuses it)
          + 256 * 4                                      // fp8 / int8 scale table
-         + 2 * kNf4Stages * 8                           // mbarriers
+         + 2 * kNf4MaxStages * 8                        // mbarriers
          + (size_t)M * r * 2;                           // staged x.A^T
 }
 
@@ -100,27 +113,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
   const int nst = (nbk + kStageBlocks - 1) / kStageBlocks;
   const int fmt = p.w.fmt;
   const bool dq = fmt != RQ_W_NF4;
+  const uint32_t S = (uint32_t)p.stages;
 
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
   unsigned char* ring = smem + 256 * 32 * 4;
-  float* sclut = reinterpret_cast<float*>(ring + kNf4Stages * STAGE);
+  float* sclut = reinterpret_cast<float*>(ring + S * STAGE);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sclut + 256);  // full[S], empty[S]
-  T* tl = reinterpret_cast<T*>(bars + 2 * kNf4Stages);
+  T* tl = reinterpret_cast<T*>(bars + 2 * kNf4MaxStages);
   float4* red = reinterpret_cast<float4*>(ring);  // after the main loop
   const uint32_t ring_s = smem_addr(ring);
-  const uint32_t full0 = smem_addr(bars), empty0 = full0 + kNf4Stages * 8;
+  const uint32_t full0 = smem_addr(bars), empty0 = full0 + kNf4MaxStages * 8;
 
-  for (int i = tid; i < 256 * 32; i += kGemvThreads) {
-    const int v = i >> 5;
-    lut[i] = pack2<DT>(kNF4[v & 15], kNF4[v >> 4]);
-  }
-  if (dq) sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
-  if (p.r > 0) {
-    const T* td = static_cast<const T*>(p.tdown);
-    for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
-  }
   if (tid == 0) {
-    for (int s = 0; s < kNf4Stages; ++s) {
+    for (uint32_t s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, kGemvWarps);
     }
@@ -152,8 +157,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
     // producer (warp 0): stage s of this chunk = blocks [8s, 8s+8) of rows
     // c0..c0+R-1, one bulk copy per row
     auto issue = [&](int s) {
-      const uint32_t gst = gs + s, slot = gst % kNf4Stages;
-      if (gst >= kNf4Stages && !mbar_wait(empty0 + 8 * slot, ((gst / kNf4Stages) + 1) & 1, abortp)) return;
+      const uint32_t gst = gs + s, slot = gst % S;
+      if (gst >= S && !mbar_wait(empty0 + 8 * slot, ((gst / S) + 1) & 1, abortp)) return;
       const int nbs = nbk - s * kStageBlocks < kStageBlocks ? nbk - s * kStageBlocks : kStageBlocks;
       const uint32_t bytes = (uint32_t)nbs * 32;
       if (lane == 0) mbar_expect_tx(full0 + 8 * slot, bytes * (uint32_t)R);
@@ -164,7 +169,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
     };
     if (warp == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // ring was written by threads (reduction)
-      for (int s = 0; s < kNf4Stages - 1 && s < nst; ++s) issue(s);
+      for (int s = 0; s < (int)S - 1 && s < nst; ++s) issue(s);
+    }
+    if (ch == 0) {
+      // tables, built while the first stages are in flight: each thread makes
+      // one code-byte entry, the warp writes the 32 copies of its 32 entries
+      const uint32_t mine = pack2<DT>(kNF4[tid & 15], kNF4[tid >> 4]);
+#pragma unroll 8
+      for (int j = 0; j < 32; ++j) lut[((warp * 32 + j) << 5) | lane] = __shfl_sync(0xffffffffu, mine, j);
+      if (dq) sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
+      if (p.r > 0) {
+        const T* td = static_cast<const T*>(p.tdown);
+        for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
+      }
+      __syncthreads();
     }
 
     // per-warp operands of the next block: X fragments and this lane's row scales
@@ -228,8 +246,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
     }
 
     for (int s = 0; s < nst; ++s) {
-      const uint32_t gst = gs + s, slot = gst % kNf4Stages;
-      if (warp == 0 && s + kNf4Stages - 1 < nst) issue(s + kNf4Stages - 1);
+      const uint32_t gst = gs + s, slot = gst % S;
+      if (warp == 0 && s + (int)S - 1 < nst) issue(s + (int)S - 1);
       const int b = s * kStageBlocks + warp;
       const bool active = b < nbk;
       const bool more = b + kStageBlocks < nbk;
@@ -239,7 +257,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
       }
       const float sA = dq ? sclut[ca] * fa : fa;
       const float sB = dq ? sclut[cb] * fb : fb;
-      const bool ok = mbar_wait(full0 + 8 * slot, (gst / kNf4Stages) & 1, abortp);
+      const bool ok = mbar_wait(full0 + 8 * slot, (gst / S) & 1, abortp);
       if (active && ok) {
         const unsigned char* stage = ring + slot * STAGE + warp * 32 + t * 8;
 #pragma unroll
@@ -286,14 +304,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
       // a wait gave up: let the copies already issued land (bounded) before
       // the ring's memory is reused or the CTA exits
       if (warp == 0)
-        for (uint32_t k = 0; k < kNf4Stages && k < gs; ++k) {
-          const uint32_t gst = gs - 1 - k, slot = gst % kNf4Stages;
+        for (uint32_t k = 0; k < S && k < gs; ++k) {
+          const uint32_t gst = gs - 1 - k, slot = gst % S;
           for (uint32_t i = 0; i < kWaitLimit; ++i) {
             uint32_t done;
             asm volatile(
                 "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
                 : "=r"(done)
-                : "r"(full0 + 8 * slot), "r"((gst / kNf4Stages) & 1)
+                : "r"(full0 + 8 * slot), "r"((gst / S) & 1)
                 : "memory");
             if (done) break;
           }
@@ -339,9 +357,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_const
 }
 
 template <int DT, int MT, int NT>
-static int nf4_launch(const GemvArgs& g, cudaStream_t st) {
+static int nf4_launch(GemvArgs g, cudaStream_t st) {
   auto kern = gemv_nf4_k<DT, MT, NT>;
-  const size_t smem = gemv_nf4_smem(NT, g.M, g.r);
+  g.stages = gemv_nf4_stages(NT, g.w.K);
+  const size_t smem = gemv_nf4_smem(NT, g.w.K, g.M, g.r);
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
   kern<<<g.grid, kGemvThreads, smem, st>>>(g);
