@@ -49,7 +49,6 @@ struct GemvArgs {
   int tiles;           // ceil(N / 8)
   int chunks;          // row chunks per CTA
   int xdt;             // activation dtype (RQ_BF16 / RQ_F16)
-  int stages;          // ring slots (NF4 streaming kernel)
 };
 
 // mma.sync m16n8k16 with a zero accumulator input (starts a block partial)
@@ -102,10 +101,10 @@ inline int num_sms() {
 
 constexpr size_t kGemvSmemCap = 113 * 1024;  // two CTAs per SM
 
-// NF4-family GEMV (gemv_nf4.cu): shared memory for a tile count, and the
-// launch for a prepared argument block.
-int gemv_nf4_stages(int nt, int64_t K);
-size_t gemv_nf4_smem(int nt, int64_t K, int64_t M, int r);
-int gemv_nf4_launch(const GemvArgs& g, int nt, cudaStream_t st);
+// NF4-family GEMV (gemv_nf4.cu): whether a shape fits its shared memory, and
+// the launch (grid and tiling chosen inside; `pdl`: launched as the
+// programmatic dependent of the LoRA down-product kernel).
+bool gemv_nf4_fits(int64_t N, int64_t K, int64_t M, int r);
+int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st);
 
 }  // namespace rq

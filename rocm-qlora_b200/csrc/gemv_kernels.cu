@@ -267,7 +267,7 @@ static size_t gemv_smem(int wk, int64_t K, int nt, int64_t M, int r) {
 
 
 static size_t smem_for(int wk, int64_t K, int nt, int64_t M, int r) {
-  return wk == 0 ? gemv_nf4_smem(nt, K, M, r) : gemv_smem(wk, K, nt, M, r);
+  return gemv_smem(wk, K, nt, M, r);
 }
 
 // Launch shape: two CTAs per SM, each owning ceil(N/8)/grid whole 8-row
@@ -296,7 +296,8 @@ bool gemv_supported(const LinearArgs& a) {
   if (a.w.K % 64 != 0 || a.w.bs != 64) return false;
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
   if (a.w.N > 0x7fffffff || a.w.K > 0x7fffffff || (a.w.N * a.w.K) / 2 > 0xfffffff0ll) return false;
-  const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
+  if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_fits(a.w.N, a.w.K, a.M, a.r);
+  const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;
   return smem_for(wk, a.w.K, 1, a.M, a.r) <= kGemvSmemCap;
 }
 
@@ -334,10 +335,10 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
   g.s = a.scaling;
   g.y = a.y;
   g.xdt = a.xdt;
-  const int wk = is_nf4_fmt(a.w.fmt) ? 0 : (a.w.fmt == RQ_W_INT8 ? 1 : 2);
+  if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_forward(g, a.r > 0, st);
+  const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;
   int nt = 1;
   gemv_shape(wk, a.w.N, a.w.K, a.M, a.r, &g.grid, &g.tiles, &g.chunks, &nt);
-  if (wk == 0) return gemv_nf4_launch(g, nt, st);
   nt = nt <= 4 ? 4 : 8;
   g.chunks = (int)(((g.tiles + g.grid - 1) / g.grid + nt - 1) / nt);
   const size_t smem = gemv_smem(wk, a.w.K, nt, a.M, a.r);

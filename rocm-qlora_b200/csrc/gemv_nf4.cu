@@ -4,388 +4,651 @@
 // LoRALinear.forward, for NF4 weights with per-block scales or with
 // double-quantized (fp8 e4m3fnuz or int8) scales.
 //
-// The code stream is the cost (N*K/2 bytes against 2*M*K bytes of X), so it
-// is moved the way HBM likes it:
+// The code stream (N*K/2 bytes) is the cost; the shared-memory data path
+// (128 bytes per clock per SM) is the second limit.  So:
 //
-//  * two CTAs per SM; CTA i owns whole 8-row tiles [T*i/G, T*(i+1)/G), i.e.
-//    one contiguous byte range of the weight (rows are contiguous);
-//  * that range streams through a 4-stage shared-memory ring with bulk
-//    asynchronous copies (cp.async.bulk, one per row and stage, 256 bytes =
-//    8 blocks of 64 codes), completed on an mbarrier per stage; consumers
-//    release a stage through a second mbarrier before it is refilled;
-//  * the 8 warps of the CTA take one 64-block of every stage each, hold fp32
-//    accumulators for all of the CTA's rows, and meet in shared memory at the
-//    end in a fixed order (deterministic);
-//  * the multiply runs on the tensor cores (mma.sync m16n8k16: X as the
-//    16-row A operand, 8 weight rows as B); code bytes become 16-bit operand
-//    pairs through a 256-entry shared table replicated 32x (one bank per
-//    lane); the block scale multiplies each block's fp32 partial;
-//  * scales are read one stage ahead per warp (one row per lane), decoded
-//    through a 256-entry fp8/int8 table, and handed to the lanes that need
-//    them with register shuffles.
+//  * CTA i owns 16-row tiles [i*TPC, (i+1)*TPC) of W (one contiguous byte
+//    range), processed in `chunks` passes of NT tiles; every CTA but the last
+//    holds the same count, so one tensor-map box size serves all;
+//  * one producer thread streams the pass through a shared-memory ring of S
+//    stages with TMA: stage s holds 64-blocks [8s, 8s+8) of the pass's rows
+//    (two 128-byte-wide boxes, 128-byte swizzle) and X's matching 512
+//    columns (one box, M rows); stage completion and release go through
+//    mbarriers (transaction bytes / consumer-warp arrivals);
+//  * 8 consumer warps: warp w multiplies block 8s + w of the stage for every
+//    tile; the warps meet in shared memory at the end in a fixed order
+//    (deterministic);
+//  * the multiply is mma.sync m16n8k16 with the weights as the A operand (16
+//    rows x 16 k) and X as B (8 tokens; two groups for M > 8), so M <= 8
+//    costs one MMA per 256 weights.  MMA row g reads tile row
+//    2*(g & 3) + (g >> 2) (and +8): with the swizzle, the 8-byte code reads
+//    of a half warp then hit 16 distinct 8-byte bank pairs;
+//  * a code byte becomes its 16-bit operand pair through a 256-entry table
+//    replicated 32 times (entry v, copy l at v*128 + l*4: lane l reads bank
+//    l), one byte permute, one multiply-add and one shared load;
+//  * block scales (fp8/int8 second level decoded) are staged in shared
+//    memory in fragment order; the scale multiplies each block's fp32
+//    partial.
 //
-// All waits are bounded.  A wait that runs out raises the CTA's abort flag
-// (every later wait then returns at once, so the kernel finishes) and
-// counts in a device counter read by rq_take_kernel_timeouts().
+// With LoRA the layer's down product x.A^T comes from the kernel launched
+// just before this one.  This kernel is then launched as its programmatic
+// dependent: it streams the weights while the down product runs and waits
+// for it (griddepcontrol.wait) only before the epilogue reads x.A^T.  Every
+// other input was written before the down-product kernel started.
+//
+// All waits are bounded: a wait that runs out raises the CTA's abort flag,
+// the CTA lets its issued copies land (bounded) and returns without writing
+// Y, and the event counts in a device counter read by
+// rq_take_kernel_timeouts().
+#include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <mutex>
+#include <vector>
 
 #include "gemv_common.cuh"
 
 namespace rq {
 
-constexpr int kNf4MaxStages = 16;
-constexpr size_t kNf4RingBudget = 72 * 1024;  // ring bytes per CTA (two CTAs per SM)
-constexpr int kStageBlocks = kGemvWarps;            // one 64-block per warp per stage
-constexpr int kRowBytes = kStageBlocks * 32;         // code bytes per row per stage
-constexpr int kRowStride = kRowBytes + 32;           // padded: conflict-free 8-byte reads
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr int kNfWarps = 8;  // consumer warps
+constexpr int kNfThreads = kNfWarps * 32;
+constexpr int kNfBlockThreads = kNfThreads + 32;  // + the producer warp
+constexpr uint32_t kWaitLimit = 1u << 22;         // polls of a barrier before a wait gives up
+constexpr uint32_t kLutBytes = 256 * 32 * 4;      // code table: 256 entries x 32 copies
+constexpr size_t kNfSmemMax = 227 * 1024 - 256;   // dynamic shared memory (static: the barriers)
+constexpr int kNfMaxNT1 = 6;                      // 16-row tiles per pass, M <= 8
+constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 8
+constexpr int kNfMaxSlots = 8;                    // ring stages
+constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one per consumer warp)
+constexpr int kLoraDownCtas = 8;                  // CTAs of the small-M down-product kernel (lora_kernels.cu)
+constexpr int kStageRegs = 24;                    // staged-scale entries a thread holds per batch
 
+// Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+struct Nf4Args {
+  CUtensorMap wmap;  // codes: uint8 [N][K/2], box 128 x NT*16, 128-byte swizzle
+  CUtensorMap xmap;  // X: 32-bit pairs [M][K/2], box 256 x M
+  GemvArgs a;
+  int tiles;         // 16-row tiles of W
+  int tpc;           // tiles per CTA (NT * chunks)
+  int chunks;        // passes per CTA
+  int stage_all;     // 1: the scales of all passes are staged once, 0: per pass
+  int sp;            // floats per block row of the staged scales (tiles held * 16 + 2)
+  int slots;         // ring stages S
+  uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X), a multiple of 1024
+  uint32_t ring_off;    // dynamic offsets: ring (rounded up to 1024 in the shared window),
+  uint32_t red_off;     //   partial sums (0: the ring itself),
+  uint32_t sc_off;      //   staged scales,
+  uint32_t aux_off;     //   256-entry second-level scale table,
+  uint32_t tl_off;      //   staged x.A^T
+};
+
+// NF4 level c (the values of kNF4) from immediates: no memory access, so the
+// table build does not wait on a cold constant cache.
+__device__ __forceinline__ float nf4_level_imm(int c) {
+  float v = -1.0f;
+  v = c == 1 ? -0.6961928009986877f : v;
+  v = c == 2 ? -0.5250730514526367f : v;
+  v = c == 3 ? -0.39491748809814453f : v;
+  v = c == 4 ? -0.28444138169288635f : v;
+  v = c == 5 ? -0.18477343022823334f : v;
+  v = c == 6 ? -0.09105003625154495f : v;
+  v = c == 7 ? 0.0f : v;
+  v = c == 8 ? 0.07958029955625534f : v;
+  v = c == 9 ? 0.16093020141124725f : v;
+  v = c == 10 ? 0.24611230194568634f : v;
+  v = c == 11 ? 0.33791524171829224f : v;
+  v = c == 12 ? 0.44070982933044434f : v;
+  v = c == 13 ? 0.5626170039176941f : v;
+  v = c == 14 ? 0.7229568362236023f : v;
+  v = c == 15 ? 1.0f : v;
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// Operand pair of code byte KB of `word` for this lane (lanesel: shared
+// address of the table plus lane*4).
+template <int KB>
+__device__ __forceinline__ uint32_t lut2(uint32_t word, uint32_t lanesel) {
+  return lds_u32(__byte_perm(word, 0u, 0x4440u | KB) * 128u + lanesel);
+}
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-
-// Waits for the phase of `bar` with the given parity to complete, at most
-// kWaitLimit polls; returns false (and raises the abort flag) if it gave up.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase of `bar` with the given parity, at most kWaitLimit
+// polls; a wait that runs out raises the CTA's abort flag (every later wait
+// then returns at once) and counts in g_kernel_timeouts.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_test(bar, parity)) return true;
     if (*abort_flag) return false;
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
   }
   *abort_flag = 1;
   atomicAdd(&g_kernel_timeouts, 1u);
   return false;
 }
+// 2-D tiled TMA load of box (x, y) of `map` into shared memory, completing on `bar`
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// barrier of the consumer warps only (the producer warp never joins it)
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNfThreads) : "memory"); }
 
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
+template <int DT, int MG>
+__device__ __forceinline__ void kstep(float (&part)[MG][4], bool first, uint32_t a0, uint32_t a1, uint32_t a2,
+                                      uint32_t a3, const uint32_t (&x)[MG][8], int j) {
+#pragma unroll
+  for (int gr = 0; gr < MG; ++gr) {
+    if (first)
+      Mma16816Zero<DT>::run(part[gr], a0, a1, a2, a3, x[gr][2 * j], x[gr][2 * j + 1]);
+    else
+      Mma16816<DT>::run(part[gr], a0, a1, a2, a3, x[gr][2 * j], x[gr][2 * j + 1]);
+  }
 }
 
-// Ring slots for a tile count: as many stages as the budget holds (the whole
-// K range when it fits), at least 2.
-int gemv_nf4_stages(int nt, int64_t K) {
-  const int64_t nst = (K / 64 + kStageBlocks - 1) / kStageBlocks;
-  int64_t s = (int64_t)(kNf4RingBudget / ((size_t)nt * 8 * kRowStride));
-  if (s > kNf4MaxStages) s = kNf4MaxStages;
-  if (s > nst) s = nst;
-  if (s < 2) s = 2;
-  return (int)s;
-}
+// tile row read by MMA row g (0..7) of a 16-row tile; rows g+8 read it + 8
+__host__ __device__ __forceinline__ int mma_row(int g) { return 2 * (g & 3) + (g >> 2); }
 
-size_t gemv_nf4_smem(int nt, int64_t K, int64_t M, int r) {
-  const int S = gemv_nf4_stages(nt, K);
-  return 256 * 32 * 4                                   // code-byte table
-         + (size_t)S * nt * 8 * kRowStride              // ring (the reduction reuses it)
-         + 256 * 4                                      // fp8 / int8 scale table
-         + 2 * kNf4MaxStages * 8                        // mbarriers
-         + (size_t)M * r * 2;                           // staged x.A^T
-}
-
-template <int DT, int MT, int NT>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_nf4_k(const __grid_constant__ GemvArgs p) {
+template <int DT, int MG, int NT>
+__global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_constant__ Nf4Args q) {
   using T = typename DType<DT>::T;
-  extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ int abort_flag;
-  constexpr int CH = NT * 8;
-  constexpr int STAGE = CH * kRowStride;
+  const GemvArgs& p = q.a;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots];  // full[S], empty[S]
+  __shared__ int abort_flag, issued, producer_done, stop;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
-  const int nbk = K / 64;
+  const int nbk = K >> 6;
   const int nst = (nbk + kStageBlocks - 1) / kStageBlocks;
-  const int fmt = p.w.fmt;
-  const bool dq = fmt != RQ_W_NF4;
-  const uint32_t S = (uint32_t)p.stages;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+  const uint32_t ring = (sbase + q.ring_off + 1023u) & ~1023u;  // shared address (swizzle atoms are 1 KB)
+  const int sp = q.sp, S = q.slots;
+  const uint32_t slot_bytes = q.slot_bytes;
+  constexpr uint32_t kBox = NT * 16 * 128;  // one 128-byte-wide code box
+  const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(bars), empty0 = full0 + kNfMaxSlots * 8;
+  volatile int* abortp = &abort_flag;
+  volatile int* issuedp = &issued;
+  volatile int* donep = &producer_done;
 
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
-  unsigned char* ring = smem + 256 * 32 * 4;
-  float* sclut = reinterpret_cast<float*>(ring + S * STAGE);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sclut + 256);  // full[S], empty[S]
-  T* tl = reinterpret_cast<T*>(bars + 2 * kNf4MaxStages);
-  float4* red = reinterpret_cast<float4*>(ring);  // after the main loop
-  const uint32_t ring_s = smem_addr(ring);
-  const uint32_t full0 = smem_addr(bars), empty0 = full0 + kNf4MaxStages * 8;
+  const int tb = blockIdx.x * q.tpc;
+  const int te = tb + q.tpc < q.tiles ? tb + q.tpc : q.tiles;
+  auto pass_tiles = [&](int ch, int& t0, int& t1) {
+    t0 = tb + ch * NT;
+    t1 = t0 + NT < te ? t0 + NT : te;
+  };
 
   if (tid == 0) {
-    for (uint32_t s = 0; s < S; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, kGemvWarps);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, kNfWarps);
     }
     abort_flag = 0;
+    issued = 0;
+    producer_done = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  const uint32_t* lut_lane = lut + lane;
 
-  const int tile_begin = (int)((int64_t)p.tiles * blockIdx.x / p.grid);
-  const int tile_end = (int)((int64_t)p.tiles * (blockIdx.x + 1) / p.grid);
-  const int ntot = tile_end - tile_begin;
-  const uint8_t* qb = static_cast<const uint8_t*>(p.w.q);
-  const T* xp = static_cast<const T*>(p.x);
-  const bool rowa = g < M, rowb = (MT == 16) && (g + 8 < M);
-  const T* xa = xp + (size_t)(rowa ? g : 0) * K + t * 16;
-  const T* xb = xp + (size_t)(rowb ? g + 8 : 0) * K + t * 16;
-  volatile int* abortp = &abort_flag;
-
-  uint32_t gs = 0;  // stages issued / consumed before this chunk (ring slot and phase)
-  for (int ch = 0; ch < p.chunks; ++ch) {
-    const int t0 = tile_begin + (int)((int64_t)ntot * ch / p.chunks);
-    const int t1 = tile_begin + (int)((int64_t)ntot * (ch + 1) / p.chunks);
-    const int ntiles = t1 - t0;
-    const int c0 = t0 * 8;
-    const int R = (t1 * 8 < N ? t1 * 8 : N) - c0;
-    if (R <= 0) break;
-
-    // producer (warp 0): stage s of this chunk = blocks [8s, 8s+8) of rows
-    // c0..c0+R-1, one bulk copy per row
-    auto issue = [&](int s) {
-      const uint32_t gst = gs + s, slot = gst % S;
-      if (gst >= S && !mbar_wait(empty0 + 8 * slot, ((gst / S) + 1) & 1, abortp)) return;
-      const int nbs = nbk - s * kStageBlocks < kStageBlocks ? nbk - s * kStageBlocks : kStageBlocks;
-      const uint32_t bytes = (uint32_t)nbs * 32;
-      if (lane == 0) mbar_expect_tx(full0 + 8 * slot, bytes * (uint32_t)R);
-      __syncwarp();
-      for (int rl = lane; rl < R; rl += 32)
-        bulk_g2s(ring_s + slot * STAGE + rl * kRowStride,
-                 qb + (size_t)(c0 + rl) * (size_t)(K / 2) + (size_t)s * kRowBytes, bytes, full0 + 8 * slot);
-    };
-    if (warp == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // ring was written by threads (reduction)
-      for (int s = 0; s < (int)S - 1 && s < nst; ++s) issue(s);
-    }
-    if (ch == 0) {
-      // tables, built while the first stages are in flight: each thread makes
-      // one code-byte entry, the warp writes the 32 copies of its 32 entries
-      const uint32_t mine = pack2<DT>(kNF4[tid & 15], kNF4[tid >> 4]);
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j) lut[((warp * 32 + j) << 5) | lane] = __shfl_sync(0xffffffffu, mine, j);
-      if (dq) sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
-      if (p.r > 0) {
-        const T* td = static_cast<const T*>(p.tdown);
-        for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
-      }
-      __syncthreads();
-    }
-
-    // per-warp operands of the next block: X fragments and this lane's row scales
-    const int ra = c0 + lane, rb = c0 + 32 + lane;
-    const bool va = lane < R, vb = 32 + lane < R;
-    auto load_x = [&](int b, uint32_t (&dst)[16]) {
-      if (rowa) {
-        const uint4* s = reinterpret_cast<const uint4*>(xa + b * 64);
-        const uint4 u0 = __ldg(s), u1 = __ldg(s + 1);
-        dst[0] = u0.x, dst[1] = u0.y, dst[2] = u0.z, dst[3] = u0.w, dst[4] = u1.x, dst[5] = u1.y, dst[6] = u1.z,
-        dst[7] = u1.w;
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = 0u;
-      }
-      if (rowb) {
-        const uint4* s = reinterpret_cast<const uint4*>(xb + b * 64);
-        const uint4 u0 = __ldg(s), u1 = __ldg(s + 1);
-        dst[8] = u0.x, dst[9] = u0.y, dst[10] = u0.z, dst[11] = u0.w, dst[12] = u1.x, dst[13] = u1.y,
-        dst[14] = u1.z, dst[15] = u1.w;
-      } else {
-#pragma unroll
-        for (int i = 8; i < 16; ++i) dst[i] = 0u;
-      }
-    };
-    // raw scale operands of block b for rows ra / rb: DQ -> (c2 byte, c2_scale), else the scale
-    auto load_sc = [&](int b, uint32_t& ca, float& fa, uint32_t& cb, float& fb) {
-      ca = cb = 0u;
-      fa = fb = 0.0f;
-      if (dq) {
-        if (va) {
-          const int64_t i = (int64_t)ra * nbk + b;
-          ca = __ldg(p.w.c2 + i);
-          fa = __ldg(p.w.c2s + (i >> 8));
-        }
-        if (NT > 4 && vb) {
-          const int64_t i = (int64_t)rb * nbk + b;
-          cb = __ldg(p.w.c2 + i);
-          fb = __ldg(p.w.c2s + (i >> 8));
-        }
-      } else {
-        if (va) fa = load_scalar(p.w.scales, p.w.sdt, (int64_t)ra * nbk + b);
-        if (NT > 4 && vb) fb = load_scalar(p.w.scales, p.w.sdt, (int64_t)rb * nbk + b);
-      }
-    };
-
-    float acc[NT][4];
-#pragma unroll
-    for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-    uint32_t xc[16], xn[16];
-    uint32_t ca, cb, na = 0, nb2 = 0;
-    float fa, fb, nfa = 0.0f, nfb = 0.0f;
-    if (warp < nbk) {
-      load_x(warp, xc);
-      load_sc(warp, ca, fa, cb, fb);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) xc[i] = 0u;
-      ca = cb = 0u;
-      fa = fb = 0.0f;
-    }
-
-    for (int s = 0; s < nst; ++s) {
-      const uint32_t gst = gs + s, slot = gst % S;
-      if (warp == 0 && s + (int)S - 1 < nst) issue(s + (int)S - 1);
-      const int b = s * kStageBlocks + warp;
-      const bool active = b < nbk;
-      const bool more = b + kStageBlocks < nbk;
-      if (more) {
-        load_x(b + kStageBlocks, xn);
-        load_sc(b + kStageBlocks, na, nfa, nb2, nfb);
-      }
-      const float sA = dq ? sclut[ca] * fa : fa;
-      const float sB = dq ? sclut[cb] * fb : fb;
-      const bool ok = mbar_wait(full0 + 8 * slot, (gst / S) & 1, abortp);
-      if (active && ok) {
-        const unsigned char* stage = ring + slot * STAGE + warp * 32 + t * 8;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          if (nt < ntiles) {
-            const uint2 cw = *reinterpret_cast<const uint2*>(stage + (nt * 8 + g) * kRowStride);
-            float part[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t word = (j < 2) ? cw.x : cw.y;
-              uint32_t b0, b1;
-              if (j & 1) {
-                b0 = lut_at<16>(word, lut_lane);
-                b1 = lut_at<24>(word, lut_lane);
-              } else {
-                b0 = lut_at<0>(word, lut_lane);
-                b1 = lut_at<8>(word, lut_lane);
-              }
-              if (j == 0)
-                Mma16816Zero<DT>::run(part, xc[0], xc[8], xc[1], xc[9], b0, b1);
-              else
-                Mma16816<DT>::run(part, xc[2 * j], xc[8 + 2 * j], xc[2 * j + 1], xc[8 + 2 * j + 1], b0, b1);
-            }
-            const float src = nt < 4 ? sA : sB;
-            const float s0 = __shfl_sync(0xffffffffu, src, (nt * 8 + 2 * t) & 31);
-            const float s1 = __shfl_sync(0xffffffffu, src, (nt * 8 + 2 * t + 1) & 31);
-            acc[nt][0] = fmaf(part[0], s0, acc[nt][0]);
-            acc[nt][1] = fmaf(part[1], s1, acc[nt][1]);
-            acc[nt][2] = fmaf(part[2], s0, acc[nt][2]);
-            acc[nt][3] = fmaf(part[3], s1, acc[nt][3]);
-          }
+  if (warp == kNfWarps) {
+    // ---- producer: stage u (over all passes) into slot u % S
+    if (lane == 0) {
+      const uint32_t bytes = 2 * kBox + (uint32_t)M * 1024;
+      uint32_t u = 0;
+      for (int ch = 0; ch < q.chunks && !*abortp; ++ch) {
+        int t0, t1;
+        pass_tiles(ch, t0, t1);
+        if (t1 <= t0) break;
+        for (int s = 0; s < nst; ++s, ++u) {
+          const uint32_t slot = u % S;
+          if (u >= (uint32_t)S && !mbar_wait(empty0 + 8 * slot, ((u / S) - 1) & 1, abortp)) break;
+          const uint32_t dst = ring + slot * slot_bytes, bar = full0 + 8 * slot;
+          mbar_expect_tx(bar, bytes);
+          tma_load_2d(dst, &q.wmap, s * 256, t0 * 16, bar);
+          tma_load_2d(dst + kBox, &q.wmap, s * 256 + 128, t0 * 16, bar);
+          tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
+          *issuedp = (int)(u + 1);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * slot);
-      if (more) {
+      __threadfence_block();
+      *donep = 1;
+    }
+    return;
+  }
+
+  // ---- consumers
+  unsigned char* lut = smem;
+  float* sc = reinterpret_cast<float*>(smem + q.sc_off);
+  float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
+  T* tl = reinterpret_cast<T*>(smem + q.tl_off);
+  const uint32_t lanesel = sbase + (uint32_t)(lane * 4);
+  // lane's code bytes in a slot: box warp >> 2, row mma_row(g) (+16 nt + 8 h),
+  // logical 16-byte chunk 2*(warp & 3) + (t >> 1) swizzled by the row, half t & 1
+  const int pg = mma_row(g);
+  const uint32_t cofs = (uint32_t)(warp >> 2) * kBox + pg * 128 +
+                        ((((2 * (warp & 3) + (t >> 1)) ^ pg) << 4) | ((t & 1) << 3));
+  // lane's X in a slot: token gr*8 + g (tokens past M read token M-1, results
+  // dropped), columns of block warp, 16 t .. 16 t + 15
+  uint32_t xofs[MG];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) xc[i] = xn[i];
-        ca = na, cb = nb2, fa = nfa, fb = nfb;
+  for (int gr = 0; gr < MG; ++gr) {
+    const int m = gr * 8 + g;
+    xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + warp * 128 + t * 32;
+  }
+
+  // scales of tiles [ta, tz) into sc (tile ta at column 0) in fragment order
+  // [block][tile][MMA row g][g / g+8].  The scales of those rows are one flat
+  // range [ta*16*nbk, ...); entry e = j*kNfThreads + tid of a batch is
+  // loaded into registers first (stage_load) and decoded and stored once the
+  // second-level table exists (stage_store).
+  const int fmt = p.w.fmt;
+  const float inv_nbk = 1.0f / (float)nbk;
+  uint32_t scv[kStageRegs];
+  float sfv[kStageRegs];
+  auto stage_load = [&](int ta, int tz, int e0) {
+    const int64_t f0 = (int64_t)ta * 16 * nbk;
+    const int total = ((tz * 16 < N ? tz * 16 : N) - ta * 16) * nbk;
+#pragma unroll
+    for (int j = 0; j < kStageRegs; ++j) {
+      const int e = e0 + j * kNfThreads + tid;
+      scv[j] = 0u;
+      sfv[j] = 0.0f;
+      if (e < total) {
+        if (fmt == RQ_W_NF4) {
+          sfv[j] = load_scalar(p.w.scales, p.w.sdt, f0 + e);
+        } else {
+          scv[j] = __ldg(p.w.c2 + f0 + e);
+          sfv[j] = __ldg(p.w.c2s + ((f0 + e) >> 8));
+        }
       }
     }
-    gs += nst;
-    if (*abortp) {
-      // a wait gave up: let the copies already issued land (bounded) before
-      // the ring's memory is reused or the CTA exits
-      if (warp == 0)
-        for (uint32_t k = 0; k < S && k < gs; ++k) {
-          const uint32_t gst = gs - 1 - k, slot = gst % S;
-          for (uint32_t i = 0; i < kWaitLimit; ++i) {
-            uint32_t done;
-            asm volatile(
-                "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-                : "=r"(done)
-                : "r"(full0 + 8 * slot), "r"((gst / S) & 1)
-                : "memory");
-            if (done) break;
-          }
-        }
-      __syncthreads();
-      return;
+  };
+  auto stage_store = [&](int ta, int tz, int e0) {
+    const int total = ((tz * 16 < N ? tz * 16 : N) - ta * 16) * nbk;
+#pragma unroll
+    for (int j = 0; j < kStageRegs; ++j) {
+      const int e = e0 + j * kNfThreads + tid;
+      if (e < total) {
+        int rl = __float2int_rz((float)e * inv_nbk), b = e - rl * nbk;
+        if (b < 0) --rl, b += nbk;
+        if (b >= nbk) ++rl, b -= nbk;
+        const int rr = rl & 15, gg = ((rr & 7) >> 1) + 4 * (rr & 1);  // MMA row of tile row rr
+        sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = fmt == RQ_W_NF4 ? sfv[j] : sclut[scv[j]] * sfv[j];
+      }
     }
+  };
+  auto stage_rest = [&](int ta, int tz, int from) {  // remaining batches, load and store each
+    const int total = ((tz * 16 < N ? tz * 16 : N) - ta * 16) * nbk;
+    for (int e0 = from; e0 < total; e0 += kStageRegs * kNfThreads) {
+      stage_load(ta, tz, e0);
+      stage_store(ta, tz, e0);
+    }
+  };
 
-    __syncthreads();  // every warp is done reading the ring; the reduction reuses it
+  int t0, t1;
+  pass_tiles(0, t0, t1);
+  const int tz0 = q.stage_all ? te : t1;
+  if (t1 > t0) stage_load(t0, tz0, 0);
+  // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])) and
+  // the second-level table, built while the first stages are in flight
+  {
+    const float lvl = nf4_level_imm(lane & 15);
+#pragma unroll
+    for (int k = 0; k < 256 * 8 / kNfThreads; ++k) {
+      const int v = k * (kNfThreads / 8) + (tid >> 3);
+      const uint32_t w = pack2<DT>(__shfl_sync(0xffffffffu, lvl, v & 15), __shfl_sync(0xffffffffu, lvl, v >> 4));
+      *reinterpret_cast<uint4*>(lut + v * 128 + (tid & 7) * 16) = make_uint4(w, w, w, w);
+    }
+  }
+  if (fmt != RQ_W_NF4)
+    sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
+  consumer_sync();
+  if (t1 > t0) {
+    stage_store(t0, tz0, 0);
+    stage_rest(t0, tz0, kStageRegs * kNfThreads);
+  }
+
+  uint32_t u = 0;  // stages consumed (over all passes)
+  for (int ch = 0; ch < q.chunks; ++ch) {
+    if (ch > 0) pass_tiles(ch, t0, t1);
+    if (t1 <= t0) break;
+    const int ntl = t1 - t0, c0 = t0 * 16;
+    const int R = (t1 * 16 < N ? t1 * 16 : N) - c0;
+    if (!q.stage_all && ch > 0) stage_rest(t0, t1, 0);
+    consumer_sync();  // scales staged
+
+    float acc[NT][MG][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
-      if (nt < ntiles)
-        red[(warp * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    __syncthreads();
+#pragma unroll
+      for (int gr = 0; gr < MG; ++gr) acc[nt][gr][0] = acc[nt][gr][1] = acc[nt][gr][2] = acc[nt][gr][3] = 0.0f;
+    const float* scw = sc + warp * sp + (q.stage_all ? t0 - tb : 0) * 16 + g * 2;
 
+    for (int s = 0; s < nst; ++s, ++u) {
+      const uint32_t slot = u % S;
+      const bool ok = mbar_wait(full0 + 8 * slot, (u / S) & 1, abortp);
+      const int b = s * kStageBlocks + warp;
+      if (ok && b < nbk) {
+        const uint32_t sl = ring + slot * slot_bytes;
+        uint32_t x[MG][8];
+#pragma unroll
+        for (int gr = 0; gr < MG; ++gr) {
+          uint4 u0, u1;
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(u0.x), "=r"(u0.y), "=r"(u0.z), "=r"(u0.w) : "r"(sl + xofs[gr]));
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(u1.x), "=r"(u1.y), "=r"(u1.z), "=r"(u1.w) : "r"(sl + xofs[gr] + 16));
+          x[gr][0] = u0.x, x[gr][1] = u0.y, x[gr][2] = u0.z, x[gr][3] = u0.w;
+          x[gr][4] = u1.x, x[gr][5] = u1.y, x[gr][6] = u1.z, x[gr][7] = u1.w;
+        }
+        const float* sb = scw + (size_t)s * kStageBlocks * sp;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          uint2 lo, hi;
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + nt * 2048));
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + nt * 2048 + 1024));
+          const float2 sv = *reinterpret_cast<const float2*>(sb + nt * 16);
+          float part[MG][4];
+          kstep<DT, MG>(part, true, lut2<0>(lo.x, lanesel), lut2<0>(hi.x, lanesel), lut2<1>(lo.x, lanesel),
+                        lut2<1>(hi.x, lanesel), x, 0);
+          kstep<DT, MG>(part, false, lut2<2>(lo.x, lanesel), lut2<2>(hi.x, lanesel), lut2<3>(lo.x, lanesel),
+                        lut2<3>(hi.x, lanesel), x, 1);
+          kstep<DT, MG>(part, false, lut2<0>(lo.y, lanesel), lut2<0>(hi.y, lanesel), lut2<1>(lo.y, lanesel),
+                        lut2<1>(hi.y, lanesel), x, 2);
+          kstep<DT, MG>(part, false, lut2<2>(lo.y, lanesel), lut2<2>(hi.y, lanesel), lut2<3>(lo.y, lanesel),
+                        lut2<3>(hi.y, lanesel), x, 3);
+#pragma unroll
+          for (int gr = 0; gr < MG; ++gr) {
+            acc[nt][gr][0] = fmaf(part[gr][0], sv.x, acc[nt][gr][0]);
+            acc[nt][gr][1] = fmaf(part[gr][1], sv.x, acc[nt][gr][1]);
+            acc[nt][gr][2] = fmaf(part[gr][2], sv.y, acc[nt][gr][2]);
+            acc[nt][gr][3] = fmaf(part[gr][3], sv.y, acc[nt][gr][3]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * slot);  // this warp is done with the slot
+    }
+
+    consumer_sync();  // every warp is done with the ring (the partial sums may reuse it)
+    if (tid == 0) stop = *abortp;  // one decision for all consumers (the producer may set the flag any time)
+    consumer_sync();
+    if (stop) break;
+    float* red = q.red_off ? reinterpret_cast<float*>(smem + q.red_off) : reinterpret_cast<float*>(smem + (ring - sbase));
+    float4* red4 = reinterpret_cast<float4*>(red);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int gr = 0; gr < MG; ++gr)
+        red4[((warp * NT + nt) * MG + gr) * 32 + lane] =
+            make_float4(acc[nt][gr][0], acc[nt][gr][1], acc[nt][gr][2], acc[nt][gr][3]);
+    if (ch == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");  // x.A^T of the kernel before
+      if (p.r > 0) {
+        const T* td = static_cast<const T*>(p.tdown);
+        for (int e = tid; e < M * p.r; e += kNfThreads) tl[e] = td[e];
+      }
+    }
+    consumer_sync();
+
+    // fragment element e of (tile nt, group gr): lane (g,t) = (e >> 2) & 31,
+    // MMA row g + 8 (e >> 1 & 1), token 8 gr + 2t + (e & 1)
     const bool has_bias = p.bias != nullptr, has_lora = p.r > 0;
     const T* lb = static_cast<const T*>(p.lora_b);
     T* y = static_cast<T*>(p.y);
-    for (int o = tid; o < CH * MT; o += kGemvThreads) {
-      const int nl = o % CH, m = o / CH;
-      if (nl >= R || m >= M) continue;
-      const int nt = nl >> 3, cc = nl & 7, tt = cc >> 1, e = cc & 1;
-      const int ln = (m & 7) * 4 + tt, comp = (m >> 3) * 2 + e;
+    for (int e = tid; e < NT * MG * 128; e += kNfThreads) {
+      const int nt = e / (MG * 128), gr = (e >> 7) % MG, ln = (e >> 2) & 31;
+      const int rl = nt * 16 + mma_row(ln >> 2) + ((e >> 1) & 1) * 8, m = gr * 8 + (ln & 3) * 2 + (e & 1);
+      if (nt >= ntl || rl >= R || m >= M) continue;
       float sum = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) {
-        const float* rv = reinterpret_cast<const float*>(&red[(w * NT + nt) * 32 + ln]);
-        sum += rv[comp];
-      }
-      const int row = c0 + nl;
-      float u = 0.0f;
+      for (int w = 0; w < kNfWarps; ++w) sum += red[w * (NT * MG * 128) + e];
+      const int row = c0 + rl;
+      float uu = 0.0f;
       if (has_lora) {
         const T* brow = lb + (size_t)row * p.r;
         const T* trow = tl + m * p.r;
 #pragma unroll 8
-        for (int j = 0; j < p.r; ++j) u = fmaf(DType<DT>::to_f32(trow[j]), DType<DT>::to_f32(__ldg(brow + j)), u);
+        for (int j = 0; j < p.r; ++j) uu = fmaf(DType<DT>::to_f32(trow[j]), DType<DT>::to_f32(__ldg(brow + j)), uu);
       }
       const float bv = has_bias ? load_scalar(p.bias, p.bdt, row) : 0.0f;
-      y[(size_t)m * N + row] = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, u, has_lora, p.s));
+      y[(size_t)m * N + row] = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, uu, has_lora, p.s));
     }
-    __syncthreads();
+    consumer_sync();  // partial sums (and per-pass scales) are reused by the next pass
+  }
+
+  if (*abortp && tid == 0) {
+    // a wait gave up: let every issued copy land (bounded) before the CTA's
+    // shared memory is released
+    for (uint32_t i = 0; i < kWaitLimit && !*donep; ++i) {
+    }
+    const uint32_t n = (uint32_t)*issuedp;
+    for (uint32_t v = u; v < n; ++v)
+      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(full0 + 8 * (v % S), (v / S) & 1); ++i) {
+      }
   }
 }
 
-template <int DT, int MT, int NT>
-static int nf4_launch(GemvArgs g, cudaStream_t st) {
-  auto kern = gemv_nf4_k<DT, MT, NT>;
-  g.stages = gemv_nf4_stages(NT, g.w.K);
-  const size_t smem = gemv_nf4_smem(NT, g.w.K, g.M, g.r);
+// ---------------------------------------------------------------- host side
+
+static size_t align16(size_t v) { return (v + 15) / 16 * 16; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda itself).
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// 2-D tensor maps, cached by (address, element type, extents, box, swizzle):
+// those determine the map completely.
+struct MapKey {
+  const void* ptr;
+  int type, swz;
+  uint64_t d0, d1, stride;
+  uint32_t b0, b1;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && type == o.type && swz == o.swz && d0 == o.d0 && d1 == o.d1 && stride == o.stride &&
+           b0 == o.b0 && b1 == o.b1;
+  }
+};
+
+static int tensor_map_2d(const MapKey& k, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::vector<std::pair<MapKey, CUtensorMap>> cache;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (const auto& e : cache)
+      if (e.first == k) {
+        *out = e.second;
+        return RQ_OK;
+      }
+  }
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return RQ_ERR_CUDA;
+  const cuuint64_t dims[2] = {k.d0, k.d1}, strides[1] = {k.stride};
+  const cuuint32_t box[2] = {k.b0, k.b1}, es[2] = {1, 1};
+  CUtensorMap m;
+  const CUresult r = enc(&m, (CUtensorMapDataType)k.type, 2, const_cast<void*>(k.ptr), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)k.swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return RQ_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() >= 4096) cache.clear();
+  cache.emplace_back(k, m);
+  *out = m;
+  return RQ_OK;
+}
+
+struct Nf4Plan {
+  int grid, tiles, tpc, chunks, nt, mg, stage_all, sp, slots;
+  size_t smem;
+  uint32_t slot_bytes, ring_off, red_off, sc_off, aux_off, tl_off;
+};
+
+// [code table | scales | second-level table | x.A^T | ring (1 KB aligned) |
+// partial sums]; with one pass the partial sums reuse the ring.
+static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
+  pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
+  size_t off = kLutBytes;
+  pl->sc_off = (uint32_t)off;
+  off += align16((size_t)nbk * pl->sp * 4);
+  pl->aux_off = (uint32_t)off;
+  off += 1024;
+  pl->tl_off = (uint32_t)off;
+  off += align16((size_t)M * (r > 0 ? r : 0) * 2);
+  pl->ring_off = (uint32_t)off;
+  off += 1024;  // room to round the ring up to a 1 KB shared address
+  const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)kNfWarps * pl->nt * pl->mg * 512;
+  if (pl->chunks == 1) {
+    pl->red_off = 0;
+    pl->smem = off + (ring > red ? ring : red);
+  } else {
+    pl->red_off = (uint32_t)(off + ring);
+    pl->smem = off + ring + red;
+  }
+  return pl->smem;
+}
+
+static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, bool pdl, Nf4Plan* pl) {
+  pl->mg = M > 8 ? 2 : 1;
+  const int64_t tiles = (N + 15) / 16;
+  // with the down product running beside it, leave the SMs its cluster uses
+  int64_t G = num_sms() - (pdl ? kLoraDownCtas : 0);
+  if (G > tiles) G = tiles;
+  if (G < 1) G = 1;
+  const int64_t per = (tiles + G - 1) / G;
+  const int64_t nbk = K / 64, nst = (nbk + kStageBlocks - 1) / kStageBlocks;
+  const int ntmax = pl->mg == 1 ? kNfMaxNT1 : kNfMaxNT2;
+  pl->tiles = (int)tiles;
+  for (int64_t ch = (per + ntmax - 1) / ntmax;; ++ch) {
+    const int64_t nt = (per + ch - 1) / ch;
+    pl->chunks = (int)ch;
+    pl->nt = (int)nt;
+    pl->tpc = (int)(nt * ch);
+    pl->grid = (int)((tiles + pl->tpc - 1) / pl->tpc);
+    // deepest ring that fits (at least 2 stages), scales of all passes at once if possible
+    for (int all = 1; all >= 0; --all) {
+      pl->stage_all = all;
+      pl->sp = (int)((all ? pl->tpc : nt) * 16 + 2);
+      for (int s = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots); s >= 2; --s) {
+        pl->slots = s;
+        if (nf4_layout(pl, nbk, M, r) <= kNfSmemMax) return true;
+      }
+    }
+    if (nt == 1) return false;
+  }
+}
+
+bool gemv_nf4_fits(int64_t N, int64_t K, int64_t M, int r) {
+  Nf4Plan pl;
+  return encode_tiled() != nullptr && nf4_plan(N, K, M, r, false, &pl) && nf4_plan(N, K, M, r, true, &pl);
+}
+
+template <int DT, int MG, int NT>
+static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) {
+  auto kern = gemv_nf4_k<DT, MG, NT>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
-  kern<<<g.grid, kGemvThreads, smem, st>>>(g);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)q.a.grid);
+  cfg.blockDim = dim3(kNfBlockThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return RQ_ERR_CUDA;
+  }
   return check_launch();
 }
 
-template <int DT, int MT>
-static int nf4_nt(const GemvArgs& g, int nt, cudaStream_t st) {
+template <int DT, int MG>
+static int nf4_nt(const Nf4Args& q, int nt, size_t smem, bool pdl, cudaStream_t st) {
   switch (nt) {
-    case 1: return nf4_launch<DT, MT, 1>(g, st);
-    case 2: return nf4_launch<DT, MT, 2>(g, st);
-    case 3: return nf4_launch<DT, MT, 3>(g, st);
-    case 4: return nf4_launch<DT, MT, 4>(g, st);
-    case 5: return nf4_launch<DT, MT, 5>(g, st);
-    case 6: return nf4_launch<DT, MT, 6>(g, st);
-    case 7: return nf4_launch<DT, MT, 7>(g, st);
-    default: return nf4_launch<DT, MT, 8>(g, st);
+    case 1: return nf4_launch<DT, MG, 1>(q, smem, pdl, st);
+    case 2: return nf4_launch<DT, MG, 2>(q, smem, pdl, st);
+    case 3: return nf4_launch<DT, MG, 3>(q, smem, pdl, st);
+    case 4: return nf4_launch<DT, MG, 4>(q, smem, pdl, st);
+    case 5: return nf4_launch<DT, MG, 5>(q, smem, pdl, st);
   }
+  if constexpr (MG == 1)
+    if (nt == 6) return nf4_launch<DT, MG, 6>(q, smem, pdl, st);
+  return RQ_ERR_INVALID;
 }
 
-int gemv_nf4_launch(const GemvArgs& g, int nt, cudaStream_t st) {
-  const bool m16 = g.M > 8;
-  if (g.w.K % 32 || ((uintptr_t)g.w.q % 16)) return RQ_ERR_ALIGN;  // bulk copies need 16-byte rows
-  if (g.xdt == RQ_BF16) return m16 ? nf4_nt<RQ_BF16, 16>(g, nt, st) : nf4_nt<RQ_BF16, 8>(g, nt, st);
-  return m16 ? nf4_nt<RQ_F16, 16>(g, nt, st) : nf4_nt<RQ_F16, 8>(g, nt, st);
+int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
+  if (g.w.K % 64 || ((uintptr_t)g.w.q % 16) || ((uintptr_t)g.x % 16)) return RQ_ERR_ALIGN;
+  Nf4Plan pl;
+  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, pdl, &pl)) return RQ_ERR_INVALID;
+  Nf4Args q;
+  // codes: bytes [N rows][K/2], box 128 x NT*16 with 128-byte swizzle;
+  // X: 32-bit element pairs [M rows][K/2], box 256 x M
+  int rc = tensor_map_2d({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, (uint64_t)(g.w.K / 2),
+                          (uint64_t)g.w.N, (uint64_t)(g.w.K / 2), 128u, (uint32_t)(pl.nt * 16)},
+                         &q.wmap);
+  if (rc == RQ_OK)
+    rc = tensor_map_2d({g.x, CU_TENSOR_MAP_DATA_TYPE_UINT32, CU_TENSOR_MAP_SWIZZLE_NONE, (uint64_t)(g.w.K / 2),
+                        (uint64_t)g.M, (uint64_t)(g.w.K * 2), 256u, (uint32_t)g.M},
+                       &q.xmap);
+  if (rc != RQ_OK) return rc;
+  q.a = g;
+  q.a.grid = pl.grid;
+  q.tiles = pl.tiles;
+  q.tpc = pl.tpc;
+  q.chunks = pl.chunks;
+  q.stage_all = pl.stage_all;
+  q.sp = pl.sp;
+  q.slots = pl.slots;
+  q.slot_bytes = pl.slot_bytes;
+  q.ring_off = pl.ring_off;
+  q.red_off = pl.red_off;
+  q.sc_off = pl.sc_off;
+  q.aux_off = pl.aux_off;
+  q.tl_off = pl.tl_off;
+  if (g.xdt == RQ_BF16)
+    return pl.mg == 2 ? nf4_nt<RQ_BF16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_BF16, 1>(q, pl.nt, pl.smem, pdl, st);
+  return pl.mg == 2 ? nf4_nt<RQ_F16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_F16, 1>(q, pl.nt, pl.smem, pdl, st);
 }
 
 }  // namespace rq

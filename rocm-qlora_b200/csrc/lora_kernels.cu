@@ -176,6 +176,8 @@ __global__ void __cluster_dims__(kLoraCluster, 1, 1) __launch_bounds__(kLoraSmal
                       const typename DType<DT>::T* __restrict__ W2, int R, float pre_s, int do_pre,
                       typename DType<DT>::T* __restrict__ out) {
   using T = typename DType<DT>::T;
+  // the layer's GEMV may start now (it reads `out` only after this grid ends)
+  asm volatile("griddepcontrol.launch_dependents;");
   constexpr int RP = NT * 8;            // padded output columns
   constexpr int KB = NT <= 4 ? 8 : 4;   // k-steps per load batch
   extern __shared__ float lsm[];
