@@ -104,7 +104,7 @@ constexpr size_t kGemvSmemCap = 113 * 1024;  // two CTAs per SM
 // NF4-family GEMV (gemv_nf4.cu): whether a shape fits its shared memory, and
 // the launch (grid and tiling chosen inside; `pdl`: launched as the
 // programmatic dependent of the LoRA down-product kernel).
-bool gemv_nf4_fits(int64_t N, int64_t K, int64_t M, int r);
+bool gemv_nf4_fits(const QWeight& w, int64_t M, int r);
 int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st);
 
 }  // namespace rq

@@ -296,7 +296,7 @@ bool gemv_supported(const LinearArgs& a) {
   if (a.w.K % 64 != 0 || a.w.bs != 64) return false;
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
   if (a.w.N > 0x7fffffff || a.w.K > 0x7fffffff || (a.w.N * a.w.K) / 2 > 0xfffffff0ll) return false;
-  if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_fits(a.w.N, a.w.K, a.M, a.r);
+  if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_fits(a.w, a.M, a.r);
   const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;
   return smem_for(wk, a.w.K, 1, a.M, a.r) <= kGemvSmemCap;
 }

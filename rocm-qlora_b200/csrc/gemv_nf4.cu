@@ -12,23 +12,28 @@
 //    holds the same count, so one tensor-map box size serves all;
 //  * one producer thread streams the pass through a shared-memory ring of S
 //    stages with TMA: stage s holds 64-blocks [8s, 8s+8) of the pass's rows
-//    (two 128-byte-wide boxes, 128-byte swizzle) and X's matching 512
-//    columns (one box, M rows); stage completion and release go through
-//    mbarriers (transaction bytes / consumer-warp arrivals);
+//    and X's matching 512 columns (one box, M rows); stage completion and
+//    release go through mbarriers (transaction bytes / consumer-warp
+//    arrivals).  The codes come as one 3-D box [128 bytes][2][rows] when
+//    K % 256 == 0 (each row's 256 contiguous bytes in one request pair, the
+//    DRAM-friendly shape), else as two 2-D 128-byte-wide boxes; both with
+//    128-byte swizzle;
 //  * 8 consumer warps: warp w multiplies block 8s + w of the stage for every
 //    tile; the warps meet in shared memory at the end in a fixed order
 //    (deterministic);
 //  * the multiply is mma.sync m16n8k16 with the weights as the A operand (16
 //    rows x 16 k) and X as B (8 tokens; two groups for M > 8), so M <= 8
-//    costs one MMA per 256 weights.  MMA row g reads tile row
-//    2*(g & 3) + (g >> 2) (and +8): with the swizzle, the 8-byte code reads
-//    of a half warp then hit 16 distinct 8-byte bank pairs;
+//    costs one MMA per 256 weights.  With the swizzle, the 8-byte code reads
+//    of a half warp hit 16 distinct 8-byte bank pairs: in the 3-D layout
+//    (shared row 2*r + half) directly, in the 2-D layout (shared row r) when
+//    MMA row g reads tile row 2*(g & 3) + (g >> 2) (and +8);
 //  * a code byte becomes its 16-bit operand pair through a 256-entry table
 //    replicated 32 times (entry v, copy l at v*128 + l*4: lane l reads bank
 //    l), one byte permute, one multiply-add and one shared load;
-//  * block scales (fp8/int8 second level decoded) are staged in shared
-//    memory in fragment order; the scale multiplies each block's fp32
-//    partial.
+//  * block scales: the producer bulk-copies each pass's raw scale bytes
+//    (c2 codes, or the plain per-block scales) into shared memory first; the
+//    consumers decode them (fp8/int8 second level times c2_scales) into
+//    fragment order; the scale multiplies each block's fp32 partial.
 //
 // With LoRA the layer's down product x.A^T comes from the kernel launched
 // just before this one.  This kernel is then launched as its programmatic
@@ -61,25 +66,27 @@ constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 
 constexpr int kNfMaxSlots = 8;                    // ring stages
 constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one per consumer warp)
 constexpr int kLoraDownCtas = 8;                  // CTAs of the small-M down-product kernel (lora_kernels.cu)
-constexpr int kStageRegs = 24;                    // staged-scale entries a thread holds per batch
 
 // Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
 
 struct Nf4Args {
-  CUtensorMap wmap;  // codes: uint8 [N][K/2], box 128 x NT*16, 128-byte swizzle
+  CUtensorMap wmap;  // codes: 3-D uint8 [N][K/256][128], box 128 x 2 x NT*16 (wide),
+                     // else 2-D uint8 [N][K/2], box 128 x NT*16; 128-byte swizzle
   CUtensorMap xmap;  // X: 32-bit pairs [M][K/2], box 256 x M
   GemvArgs a;
   int tiles;         // 16-row tiles of W
   int tpc;           // tiles per CTA (NT * chunks)
   int chunks;        // passes per CTA
-  int stage_all;     // 1: the scales of all passes are staged once, 0: per pass
-  int sp;            // floats per block row of the staged scales (tiles held * 16 + 2)
+  int sp;            // floats per block row of the staged scales (NT * 16 + 2)
+  int esz;           // bytes per raw scale (1: c2 codes; 2/4: plain scales)
+  int wide;          // 1: 3-D code box (K % 256 == 0)
   int slots;         // ring stages S
   uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X), a multiple of 1024
   uint32_t ring_off;    // dynamic offsets: ring (rounded up to 1024 in the shared window),
   uint32_t red_off;     //   partial sums (0: the ring itself),
-  uint32_t sc_off;      //   staged scales,
+  uint32_t sc_off;      //   decoded scales of a pass,
+  uint32_t raw_off;     //   raw scale bytes of a pass, c2_scales of a pass,
   uint32_t aux_off;     //   256-entry second-level scale table,
   uint32_t tl_off;      //   staged x.A^T
 };
@@ -157,6 +164,19 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "l"(map), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
+// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16), completing on `bar`
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
 // barrier of the consumer warps only (the producer warp never joins it)
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNfThreads) : "memory"); }
 
@@ -172,16 +192,19 @@ __device__ __forceinline__ void kstep(float (&part)[MG][4], bool first, uint32_t
   }
 }
 
-// tile row read by MMA row g (0..7) of a 16-row tile; rows g+8 read it + 8
-__host__ __device__ __forceinline__ int mma_row(int g) { return 2 * (g & 3) + (g >> 2); }
+// tile row read by MMA row g (0..7) of a 16-row tile (rows g+8 read it + 8):
+// the identity in the 3-D layout, a permutation in the 2-D one
+__host__ __device__ __forceinline__ int mma_row(int g, int wide) { return wide ? g : 2 * (g & 3) + (g >> 2); }
+// MMA row of tile row rr (0..15) modulo 8
+__host__ __device__ __forceinline__ int mma_of_row(int rr, int wide) { return wide ? (rr & 7) : ((rr & 7) >> 1) + 4 * (rr & 1); }
 
 template <int DT, int MG, int NT>
 __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_constant__ Nf4Args q) {
   using T = typename DType<DT>::T;
   const GemvArgs& p = q.a;
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots];  // full[S], empty[S]
-  __shared__ int abort_flag, issued, producer_done, stop;
+  __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots + 2];  // full[S], empty[S], scales full / empty
+  __shared__ int abort_flag, issued, raw_issued, producer_done, stop;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
   const int nbk = K >> 6;
@@ -192,8 +215,15 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   const uint32_t slot_bytes = q.slot_bytes;
   constexpr uint32_t kBox = NT * 16 * 128;  // one 128-byte-wide code box
   const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(bars), empty0 = full0 + kNfMaxSlots * 8;
+  const uint32_t scfull = full0 + 2 * kNfMaxSlots * 8, scempty = scfull + 8;
+  // raw scale bytes of the pass at rows [c0, c0+R): one copy of the 16-byte
+  // aligned part (the rest, under 16 bytes, is read directly)
+  const int esz = q.esz;
+  const unsigned char* rawsrc = static_cast<const unsigned char*>(p.w.fmt == RQ_W_NF4 ? p.w.scales : (const void*)p.w.c2);
+  auto raw_bytes = [&](int R) { return (uint32_t)(R * nbk * esz) & ~15u; };
   volatile int* abortp = &abort_flag;
   volatile int* issuedp = &issued;
+  volatile int* raw_issuedp = &raw_issued;
   volatile int* donep = &producer_done;
 
   const int tb = blockIdx.x * q.tpc;
@@ -208,8 +238,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       mbar_init(full0 + 8 * i, 1);
       mbar_init(empty0 + 8 * i, kNfWarps);
     }
+    mbar_init(scfull, 1);
+    mbar_init(scempty, 1);
     abort_flag = 0;
     issued = 0;
+    raw_issued = 0;
     producer_done = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -224,13 +257,25 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         int t0, t1;
         pass_tiles(ch, t0, t1);
         if (t1 <= t0) break;
+        // the pass's raw scales first (the buffer is free once the consumers
+        // decoded the previous pass's)
+        if (ch > 0 && !mbar_wait(scempty, (ch - 1) & 1, abortp)) break;
+        const int R = (t1 * 16 < N ? t1 * 16 : N) - t0 * 16;
+        const uint32_t rb = raw_bytes(R);
+        mbar_expect_tx(scfull, rb);
+        if (rb) bulk_load(sbase + q.raw_off, rawsrc + (size_t)t0 * 16 * nbk * esz, rb, scfull);
+        *raw_issuedp = ch + 1;
         for (int s = 0; s < nst; ++s, ++u) {
           const uint32_t slot = u % S;
           if (u >= (uint32_t)S && !mbar_wait(empty0 + 8 * slot, ((u / S) - 1) & 1, abortp)) break;
           const uint32_t dst = ring + slot * slot_bytes, bar = full0 + 8 * slot;
           mbar_expect_tx(bar, bytes);
-          tma_load_2d(dst, &q.wmap, s * 256, t0 * 16, bar);
-          tma_load_2d(dst + kBox, &q.wmap, s * 256 + 128, t0 * 16, bar);
+          if (q.wide) {
+            tma_load_3d(dst, &q.wmap, 0, 2 * s, t0 * 16, bar);
+          } else {
+            tma_load_2d(dst, &q.wmap, s * 256, t0 * 16, bar);
+            tma_load_2d(dst + kBox, &q.wmap, s * 256 + 128, t0 * 16, bar);
+          }
           tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
           *issuedp = (int)(u + 1);
         }
@@ -247,11 +292,16 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
   T* tl = reinterpret_cast<T*>(smem + q.tl_off);
   const uint32_t lanesel = sbase + (uint32_t)(lane * 4);
-  // lane's code bytes in a slot: box warp >> 2, row mma_row(g) (+16 nt + 8 h),
-  // logical 16-byte chunk 2*(warp & 3) + (t >> 1) swizzled by the row, half t & 1
-  const int pg = mma_row(g);
-  const uint32_t cofs = (uint32_t)(warp >> 2) * kBox + pg * 128 +
-                        ((((2 * (warp & 3) + (t >> 1)) ^ pg) << 4) | ((t & 1) << 3));
+  // lane's code bytes in a slot: logical 16-byte chunk 2*(warp & 3) + (t >> 1)
+  // of 128-byte half warp >> 2 of tile row mma_row(g) (+16 nt + 8 h), half t & 1;
+  // the 128-byte shared rows are swizzled by their index mod 8.
+  //   3-D: shared row 2*r + half -> per tile 4096 bytes, per h 2048
+  //   2-D: half at kBox, shared row r -> per tile 2048 bytes, per h 1024
+  const int wide = q.wide;
+  const int pg = mma_row(g, wide), half = warp >> 2, lch = 2 * (warp & 3) + (t >> 1);
+  const uint32_t cofs = wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
+                             : (uint32_t)half * kBox + pg * 128 + (((lch ^ pg) << 4) | ((t & 1) << 3));
+  const uint32_t tstep = wide ? 4096u : 2048u, hstep = tstep / 2;
   // lane's X in a slot: token gr*8 + g (tokens past M read token M-1, results
   // dropped), columns of block warp, 16 t .. 16 t + 15
   uint32_t xofs[MG];
@@ -261,64 +311,47 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + warp * 128 + t * 32;
   }
 
-  // scales of tiles [ta, tz) into sc (tile ta at column 0) in fragment order
-  // [block][tile][MMA row g][g / g+8].  The scales of those rows are one flat
-  // range [ta*16*nbk, ...); entry e = j*kNfThreads + tid of a batch is
-  // loaded into registers first (stage_load) and decoded and stored once the
-  // second-level table exists (stage_store).
+  // decoded scales of the pass at rows [c0, c0+R) into sc in fragment order
+  // [block][tile][MMA row g][g / g+8]
   const int fmt = p.w.fmt;
   const float inv_nbk = 1.0f / (float)nbk;
-  uint32_t scv[kStageRegs];
-  float sfv[kStageRegs];
-  auto stage_load = [&](int ta, int tz, int e0) {
-    const int64_t f0 = (int64_t)ta * 16 * nbk;
-    const int total = ((tz * 16 < N ? tz * 16 : N) - ta * 16) * nbk;
-#pragma unroll
-    for (int j = 0; j < kStageRegs; ++j) {
-      const int e = e0 + j * kNfThreads + tid;
-      scv[j] = 0u;
-      sfv[j] = 0.0f;
-      if (e < total) {
-        if (fmt == RQ_W_NF4) {
-          sfv[j] = load_scalar(p.w.scales, p.w.sdt, f0 + e);
-        } else {
-          scv[j] = __ldg(p.w.c2 + f0 + e);
-          sfv[j] = __ldg(p.w.c2s + ((f0 + e) >> 8));
-        }
-      }
-    }
+  const unsigned char* raw = smem + q.raw_off;
+  float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
+  auto c2s_load = [&](int c0, int R) {  // the pass's c2_scales (one per 256 blocks)
+    if (fmt == RQ_W_NF4) return;
+    const int64_t f0 = (int64_t)c0 * nbk;
+    const int n = (int)(((f0 + (int64_t)R * nbk - 1) >> 8) - (f0 >> 8)) + 1;
+    for (int i = tid; i < n; i += kNfThreads) c2s_sm[i] = __ldg(p.w.c2s + (f0 >> 8) + i);
   };
-  auto stage_store = [&](int ta, int tz, int e0) {
-    const int total = ((tz * 16 < N ? tz * 16 : N) - ta * 16) * nbk;
-#pragma unroll
-    for (int j = 0; j < kStageRegs; ++j) {
-      const int e = e0 + j * kNfThreads + tid;
-      if (e < total) {
-        int rl = __float2int_rz((float)e * inv_nbk), b = e - rl * nbk;
-        if (b < 0) --rl, b += nbk;
-        if (b >= nbk) ++rl, b -= nbk;
-        const int rr = rl & 15, gg = ((rr & 7) >> 1) + 4 * (rr & 1);  // MMA row of tile row rr
-        sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = fmt == RQ_W_NF4 ? sfv[j] : sclut[scv[j]] * sfv[j];
+  auto decode = [&](int c0, int R) {
+    const int64_t f0 = (int64_t)c0 * nbk;
+    const int total = R * nbk, inraw = (int)(raw_bytes(R) / esz);
+    for (int e = tid; e < total; e += kNfThreads) {
+      int rl = __float2int_rz((float)e * inv_nbk), b = e - rl * nbk;
+      if (b < 0) --rl, b += nbk;
+      if (b >= nbk) ++rl, b -= nbk;
+      float v;
+      if (fmt == RQ_W_NF4) {
+        v = e < inraw ? (esz == 4 ? reinterpret_cast<const float*>(raw)[e]
+                                  : load_scalar(raw, p.w.sdt, e))
+                      : load_scalar(p.w.scales, p.w.sdt, f0 + e);
+      } else {
+        const uint32_t c = e < inraw ? raw[e] : __ldg(p.w.c2 + f0 + e);
+        v = sclut[c] * c2s_sm[((f0 + e) >> 8) - (f0 >> 8)];
       }
-    }
-  };
-  auto stage_rest = [&](int ta, int tz, int from) {  // remaining batches, load and store each
-    const int total = ((tz * 16 < N ? tz * 16 : N) - ta * 16) * nbk;
-    for (int e0 = from; e0 < total; e0 += kStageRegs * kNfThreads) {
-      stage_load(ta, tz, e0);
-      stage_store(ta, tz, e0);
+      const int rr = rl & 15, gg = mma_of_row(rr, q.wide);
+      sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = v;
     }
   };
 
   int t0, t1;
   pass_tiles(0, t0, t1);
-  const int tz0 = q.stage_all ? te : t1;
-  if (t1 > t0) stage_load(t0, tz0, 0);
+  if (t1 > t0) c2s_load(t0 * 16, (t1 * 16 < N ? t1 * 16 : N) - t0 * 16);
   // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])) and
   // the second-level table, built while the first stages are in flight
   {
     const float lvl = nf4_level_imm(lane & 15);
-#pragma unroll
+#pragma unroll 1
     for (int k = 0; k < 256 * 8 / kNfThreads; ++k) {
       const int v = k * (kNfThreads / 8) + (tid >> 3);
       const uint32_t w = pack2<DT>(__shfl_sync(0xffffffffu, lvl, v & 15), __shfl_sync(0xffffffffu, lvl, v >> 4));
@@ -327,27 +360,29 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   }
   if (fmt != RQ_W_NF4)
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
-  consumer_sync();
-  if (t1 > t0) {
-    stage_store(t0, tz0, 0);
-    stage_rest(t0, tz0, kStageRegs * kNfThreads);
-  }
 
-  uint32_t u = 0;  // stages consumed (over all passes)
+  uint32_t u = 0;       // stages consumed (over all passes)
+  uint32_t passes = 0;  // raw-scale copies waited for
   for (int ch = 0; ch < q.chunks; ++ch) {
     if (ch > 0) pass_tiles(ch, t0, t1);
     if (t1 <= t0) break;
     const int ntl = t1 - t0, c0 = t0 * 16;
     const int R = (t1 * 16 < N ? t1 * 16 : N) - c0;
-    if (!q.stage_all && ch > 0) stage_rest(t0, t1, 0);
-    consumer_sync();  // scales staged
+    if (ch > 0) c2s_load(c0, R);
+    consumer_sync();  // tables and c2_scales in place
+    // the pass's raw scales have landed: decode them, then hand the buffer back
+    mbar_wait(scfull, ch & 1, abortp);
+    ++passes;
+    decode(c0, R);
+    consumer_sync();
+    if (tid == 0) mbar_arrive(scempty);
 
     float acc[NT][MG][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int gr = 0; gr < MG; ++gr) acc[nt][gr][0] = acc[nt][gr][1] = acc[nt][gr][2] = acc[nt][gr][3] = 0.0f;
-    const float* scw = sc + warp * sp + (q.stage_all ? t0 - tb : 0) * 16 + g * 2;
+    const float* scw = sc + warp * sp + g * 2;
 
     for (int s = 0; s < nst; ++s, ++u) {
       const uint32_t slot = u % S;
@@ -368,8 +403,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           uint2 lo, hi;
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + nt * 2048));
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + nt * 2048 + 1024));
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + nt * tstep));
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + nt * tstep + hstep));
           const float2 sv = *reinterpret_cast<const float2*>(sb + nt * 16);
           float part[MG][4];
           kstep<DT, MG>(part, true, lut2<0>(lo.x, lanesel), lut2<0>(hi.x, lanesel), lut2<1>(lo.x, lanesel),
@@ -421,7 +456,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     T* y = static_cast<T*>(p.y);
     for (int e = tid; e < NT * MG * 128; e += kNfThreads) {
       const int nt = e / (MG * 128), gr = (e >> 7) % MG, ln = (e >> 2) & 31;
-      const int rl = nt * 16 + mma_row(ln >> 2) + ((e >> 1) & 1) * 8, m = gr * 8 + (ln & 3) * 2 + (e & 1);
+      const int rl = nt * 16 + mma_row(ln >> 2, wide) + ((e >> 1) & 1) * 8, m = gr * 8 + (ln & 3) * 2 + (e & 1);
       if (nt >= ntl || rl >= R || m >= M) continue;
       float sum = 0.0f;
 #pragma unroll
@@ -445,9 +480,12 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // shared memory is released
     for (uint32_t i = 0; i < kWaitLimit && !*donep; ++i) {
     }
-    const uint32_t n = (uint32_t)*issuedp;
+    const uint32_t n = (uint32_t)*issuedp, nr = (uint32_t)*raw_issuedp;
     for (uint32_t v = u; v < n; ++v)
       for (uint32_t i = 0; i < kWaitLimit && !mbar_test(full0 + 8 * (v % S), (v / S) & 1); ++i) {
+      }
+    for (uint32_t v = passes; v < nr; ++v)
+      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, v & 1); ++i) {
       }
   }
 }
@@ -475,20 +513,21 @@ static EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// 2-D tensor maps, cached by (address, element type, extents, box, swizzle):
+// 2-D / 3-D tensor maps, cached by (address, element type, extents, box, swizzle):
 // those determine the map completely.
 struct MapKey {
   const void* ptr;
-  int type, swz;
-  uint64_t d0, d1, stride;
-  uint32_t b0, b1;
+  int type, swz, rank;
+  uint64_t d[3], stride[2];
+  uint32_t box[3];
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && type == o.type && swz == o.swz && d0 == o.d0 && d1 == o.d1 && stride == o.stride &&
-           b0 == o.b0 && b1 == o.b1;
+    return ptr == o.ptr && type == o.type && swz == o.swz && rank == o.rank && d[0] == o.d[0] && d[1] == o.d[1] &&
+           d[2] == o.d[2] && stride[0] == o.stride[0] && stride[1] == o.stride[1] && box[0] == o.box[0] &&
+           box[1] == o.box[1] && box[2] == o.box[2];
   }
 };
 
-static int tensor_map_2d(const MapKey& k, CUtensorMap* out) {
+static int tensor_map(const MapKey& k, CUtensorMap* out) {
   static std::mutex mu;
   static std::vector<std::pair<MapKey, CUtensorMap>> cache;
   {
@@ -501,10 +540,10 @@ static int tensor_map_2d(const MapKey& k, CUtensorMap* out) {
   }
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return RQ_ERR_CUDA;
-  const cuuint64_t dims[2] = {k.d0, k.d1}, strides[1] = {k.stride};
-  const cuuint32_t box[2] = {k.b0, k.b1}, es[2] = {1, 1};
+  const cuuint64_t dims[3] = {k.d[0], k.d[1], k.d[2]}, strides[2] = {k.stride[0], k.stride[1]};
+  const cuuint32_t box[3] = {k.box[0], k.box[1], k.box[2]}, es[3] = {1, 1, 1};
   CUtensorMap m;
-  const CUresult r = enc(&m, (CUtensorMapDataType)k.type, 2, const_cast<void*>(k.ptr), dims, strides, box, es,
+  const CUresult r = enc(&m, (CUtensorMapDataType)k.type, (cuuint32_t)k.rank, const_cast<void*>(k.ptr), dims, strides, box, es,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)k.swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return RQ_ERR_INVALID;
@@ -516,18 +555,21 @@ static int tensor_map_2d(const MapKey& k, CUtensorMap* out) {
 }
 
 struct Nf4Plan {
-  int grid, tiles, tpc, chunks, nt, mg, stage_all, sp, slots;
+  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
   size_t smem;
-  uint32_t slot_bytes, ring_off, red_off, sc_off, aux_off, tl_off;
+  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off;
 };
 
-// [code table | scales | second-level table | x.A^T | ring (1 KB aligned) |
-// partial sums]; with one pass the partial sums reuse the ring.
+// [code table | scales | raw scales + c2_scales of a pass | second-level
+// table | x.A^T | ring (1 KB aligned) | partial sums]; with one pass the
+// partial sums reuse the ring.
 static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
   size_t off = kLutBytes;
   pl->sc_off = (uint32_t)off;
   off += align16((size_t)nbk * pl->sp * 4);
+  pl->raw_off = (uint32_t)off;
+  off += align16((size_t)pl->nt * 16 * nbk * pl->esz) + align16(((size_t)pl->nt * 16 * nbk / 256 + 2) * 4);
   pl->aux_off = (uint32_t)off;
   off += 1024;
   pl->tl_off = (uint32_t)off;
@@ -545,8 +587,9 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   return pl->smem;
 }
 
-static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, bool pdl, Nf4Plan* pl) {
+static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool pdl, Nf4Plan* pl) {
   pl->mg = M > 8 ? 2 : 1;
+  pl->esz = esz;
   const int64_t tiles = (N + 15) / 16;
   // with the down product running beside it, leave the SMs its cluster uses
   int64_t G = num_sms() - (pdl ? kLoraDownCtas : 0);
@@ -562,22 +605,27 @@ static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, bool pdl, Nf4Plan* 
     pl->nt = (int)nt;
     pl->tpc = (int)(nt * ch);
     pl->grid = (int)((tiles + pl->tpc - 1) / pl->tpc);
-    // deepest ring that fits (at least 2 stages), scales of all passes at once if possible
-    for (int all = 1; all >= 0; --all) {
-      pl->stage_all = all;
-      pl->sp = (int)((all ? pl->tpc : nt) * 16 + 2);
-      for (int s = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots); s >= 2; --s) {
-        pl->slots = s;
-        if (nf4_layout(pl, nbk, M, r) <= kNfSmemMax) return true;
-      }
+    // deepest ring that fits (at least 2 stages)
+    pl->sp = (int)(nt * 16 + 2);
+    for (int s = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots); s >= 2; --s) {
+      pl->slots = s;
+      if (nf4_layout(pl, nbk, M, r) <= kNfSmemMax) return true;
     }
     if (nt == 1) return false;
   }
 }
 
-bool gemv_nf4_fits(int64_t N, int64_t K, int64_t M, int r) {
+// bytes per raw scale entry of the weight's format
+static int nf4_esz(const QWeight& w) {
+  if (w.fmt != RQ_W_NF4) return 1;
+  return w.sdt == RQ_F32 ? 4 : 2;
+}
+
+bool gemv_nf4_fits(const QWeight& w, int64_t M, int r) {
   Nf4Plan pl;
-  return encode_tiled() != nullptr && nf4_plan(N, K, M, r, false, &pl) && nf4_plan(N, K, M, r, true, &pl);
+  const void* sp = w.fmt == RQ_W_NF4 ? w.scales : (const void*)w.c2;
+  return encode_tiled() != nullptr && ((uintptr_t)sp % 16) == 0 && nf4_plan(w.N, w.K, M, r, nf4_esz(w), false, &pl) &&
+         nf4_plan(w.N, w.K, M, r, nf4_esz(w), true, &pl);
 }
 
 template <int DT, int MG, int NT>
@@ -620,30 +668,37 @@ static int nf4_nt(const Nf4Args& q, int nt, size_t smem, bool pdl, cudaStream_t 
 int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   if (g.w.K % 64 || ((uintptr_t)g.w.q % 16) || ((uintptr_t)g.x % 16)) return RQ_ERR_ALIGN;
   Nf4Plan pl;
-  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, pdl, &pl)) return RQ_ERR_INVALID;
+  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), pdl, &pl)) return RQ_ERR_INVALID;
   Nf4Args q;
-  // codes: bytes [N rows][K/2], box 128 x NT*16 with 128-byte swizzle;
+  // codes with 128-byte swizzle: 3-D [N][K/256][128] bytes, box 128 x 2 x NT*16
+  // when K % 256 == 0, else 2-D [N][K/2] bytes, box 128 x NT*16;
   // X: 32-bit element pairs [M rows][K/2], box 256 x M
-  int rc = tensor_map_2d({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, (uint64_t)(g.w.K / 2),
-                          (uint64_t)g.w.N, (uint64_t)(g.w.K / 2), 128u, (uint32_t)(pl.nt * 16)},
-                         &q.wmap);
+  const uint64_t rowb = (uint64_t)(g.w.K / 2), rows = (uint64_t)g.w.N, nt16 = (uint64_t)(pl.nt * 16);
+  q.wide = g.w.K % 256 == 0;
+  int rc = q.wide ? tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 3,
+                                {128, rowb / 128, rows}, {128, rowb}, {128u, 2u, (uint32_t)nt16}},
+                               &q.wmap)
+                  : tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 2,
+                                {rowb, rows, 1}, {rowb, 0}, {128u, (uint32_t)nt16, 1u}},
+                               &q.wmap);
   if (rc == RQ_OK)
-    rc = tensor_map_2d({g.x, CU_TENSOR_MAP_DATA_TYPE_UINT32, CU_TENSOR_MAP_SWIZZLE_NONE, (uint64_t)(g.w.K / 2),
-                        (uint64_t)g.M, (uint64_t)(g.w.K * 2), 256u, (uint32_t)g.M},
-                       &q.xmap);
+    rc = tensor_map({g.x, CU_TENSOR_MAP_DATA_TYPE_UINT32, CU_TENSOR_MAP_SWIZZLE_NONE, 2,
+                     {rowb, (uint64_t)g.M, 1}, {(uint64_t)(g.w.K * 2), 0}, {256u, (uint32_t)g.M, 1u}},
+                    &q.xmap);
   if (rc != RQ_OK) return rc;
   q.a = g;
   q.a.grid = pl.grid;
   q.tiles = pl.tiles;
   q.tpc = pl.tpc;
   q.chunks = pl.chunks;
-  q.stage_all = pl.stage_all;
   q.sp = pl.sp;
+  q.esz = pl.esz;
   q.slots = pl.slots;
   q.slot_bytes = pl.slot_bytes;
   q.ring_off = pl.ring_off;
   q.red_off = pl.red_off;
   q.sc_off = pl.sc_off;
+  q.raw_off = pl.raw_off;
   q.aux_off = pl.aux_off;
   q.tl_off = pl.tl_off;
   if (g.xdt == RQ_BF16)

@@ -101,10 +101,11 @@ def _oracle_y_dx(lora, x, dy):
     return y, dx
 
 
-@pytest.mark.parametrize("N,K", [(4096, 4096), (1000, 2048), (264, 11008)])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (1000, 2048), (264, 11008), (600, 1088), (40, 320)])
 @pytest.mark.parametrize("M", [1, 4, 5, 16])
 def test_decode_gemv_nf4_dq_vs_oracle(N, K, M):
-    """Decode shapes (GEMV path) with double-quantized NF4, r=16 alpha=32."""
+    """Decode shapes (GEMV path) with double-quantized NF4, r=16 alpha=32.
+    K = 1088 and 320 are not multiples of 256 (the narrow code layout)."""
     inp = layer_inputs(N, K, M, sigma=0.02, r=16, alpha=32, seed=N + K + M, with_dy=True)
     lora = build_layer(inp.W, 4, True, None, inp.r, inp.alpha, inp.A, inp.B)
     x = inp.X.cuda().requires_grad_(True)
