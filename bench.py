@@ -5,8 +5,9 @@ projections W[N, K] in {4096x4096, 11008x4096, 4096x11008}, bf16 N(0, 0.02)
 weights quantized to NF4 with double-quantized scales (block 64, fp8
 second level over 256 blocks), X in {1, 4, 16} x K bf16 N(0, 1), LoRA r=16
 alpha=32 with B ~ N(0, 0.01).  One step = the nine LoRALinear forwards of
-the sweep.  Metric: HBM GB/s of algorithmic bytes (SURVEY 8d formula:
-N*K/2 + nb + 4*ceil(nb/256) + 2MK + 2MN + 2r(K+N) per call).
+the sweep.  Metric: HBM GB/s of algorithmic bytes per call:
+N*K/2 (codes) + nb (fp8 second-level codes, nb = N*K/64 blocks) +
+4*ceil(nb/256) (second-level scales) + 2MK (X) + 2MN (Y) + 2r(K+N) (A, B).
 
 The weight set is replicated over >= 512 MB of distinct copies and each step
 reads the next copy, so every call streams its weights from HBM (the 126 MB
@@ -16,8 +17,11 @@ copy) and timed with CUDA events; multi-GPU runs time the max over ranks.
 Arms:
   python bench.py [--gpus N] [--steps K] [--warmup W]   the B200 kernels
   python bench.py --impl reference ...                  the reference's CPU
-      path as restated by the oracle (C dequantize + numpy matmul), on this
+      path (its eager torch ops, restated in oracle/torch_port.py) on this
       host's cores, over a bounded sample of the same workload.
+The clock sampler (nvidia-smi, 100 ms) runs over untimed load steps right
+before the timed region as well as during it, so short timed regions still
+get samples under load.
 With N > 1 (torchrun), each rank holds a column shard: the sweep's layers
 have N times the output features, every rank runs its [N_shape, K] shard,
 and Y is all-gathered over NCCL (weak scaling).
@@ -227,6 +231,11 @@ def run_ours(args, rank, world, device):
 
     run_steps(args.warmup, 0, True, graphs)
     with ClockSampler(device.index) as clk:
+        # untimed load for the sampler (about 0.4 s), then the timed steps
+        t_end = time.perf_counter() + 0.4
+        while time.perf_counter() < t_end:
+            run_steps(50, 0, True, graphs)
+            torch.cuda.synchronize(device)
         ms = timed(args.steps, True, graphs)
     clocks = clk.summary()
     step_bytes = sum(algo_bytes(SHAPES[si][0], SHAPES[si][1], M, R) for si, M in calls)
@@ -270,7 +279,7 @@ def run_ours(args, rank, world, device):
                        "graphs": use_graphs},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "gemv_k (fused NF4-DQ dequant GEMV, no adapter)",
+                         "kernel": "gemv_nf4_k (fused NF4-DQ dequant GEMV, no adapter)",
                          "launches": n_launch, "us_per_launch": round(ms_g * 1e3 / n_launch, 3)},
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -471,8 +480,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="single-layer run for profiling, e.g. decode:11008:4096:16")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
