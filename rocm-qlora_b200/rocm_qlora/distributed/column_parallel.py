@@ -1,0 +1,146 @@
+"""Column-sharded QuantLinear (+ LoRA) across the GPUs of one node.
+
+The quantized weight W [N, K] is split by output features into contiguous
+row ranges, 16 rows apiece where possible (blocks stay whole: with K % 64
+== 0 a 64-block never crosses a row).  Rank i holds rows [lo_i, hi_i) of W,
+of the bias and of LoRA B; LoRA A [r, K] is replicated.
+
+  forward    Y_i = layer_i(X);  Y = all-gather of the Y_i over the features
+  backward   dX  = sum over ranks of dX_i  (all-reduce)
+             dA  = sum over ranks of dA_i  (all-reduce; A is replicated)
+             dB_i, dbias_i stay local
+
+The collectives are NCCL over NVLink (torch.distributed); the per-rank
+layer is the fused B200 QuantLinear / LoRALinear of this package.
+"""
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from rocm_qlora.lora.lora_layer import LoRALinear
+from rocm_qlora.quantization.quant_linear import QuantLinear
+
+
+def shard_range(n: int, world: int, rank: int, granule: int = 16) -> Tuple[int, int]:
+    """Rows [lo, hi) of `rank` when `n` rows are split over `world` ranks in
+    units of `granule` rows (the last unit may be short); shard sizes differ
+    by at most one unit."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    units = -(-n // granule)
+    lo = units * rank // world * granule
+    hi = units * (rank + 1) // world * granule
+    return min(lo, n), min(hi, n)
+
+
+def _world(group) -> Tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+class _ReduceGradient(torch.autograd.Function):
+    """Identity forward; the gradient is summed over the group (the input is
+    replicated, every rank's shard contributes to its gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        dist.all_reduce(g, group=ctx.group)
+        return g, None
+
+
+class _GatherFeatures(torch.autograd.Function):
+    """All-gather of the ranks' output features along the last dimension;
+    the gradient of each rank is its own slice."""
+
+    @staticmethod
+    def forward(ctx, y, group, sizes: List[int], rank: int):
+        ctx.lo = sum(sizes[:rank])
+        ctx.n = sizes[rank]
+        nmax = max(sizes)
+        lead = y.shape[:-1]
+        y2 = y.reshape(-1, y.shape[-1])
+        if y2.shape[1] < nmax:  # uneven shards: pad to the largest
+            y2 = torch.nn.functional.pad(y2, (0, nmax - y2.shape[1]))
+        buf = torch.empty((len(sizes), y2.shape[0], nmax), dtype=y.dtype, device=y.device)
+        if dist.get_backend(group) == "nccl":
+            dist.all_gather_into_tensor(buf, y2.contiguous(), group=group)
+        else:  # gloo has no single-buffer all-gather
+            dist.all_gather(list(buf.unbind(0)), y2.contiguous(), group=group)
+        out = torch.cat([buf[i, :, :sizes[i]] for i in range(len(sizes))], dim=1)
+        return out.reshape(*lead, sum(sizes))
+
+    @staticmethod
+    def backward(ctx, g):
+        return g[..., ctx.lo:ctx.lo + ctx.n].contiguous(), None, None, None
+
+
+class ColumnParallelLinear(nn.Module):
+    """One rank's shard of a column-sharded layer.
+
+    `local` computes this rank's output features (a QuantLinear or
+    LoRALinear over rows [lo, hi) of the full weight); `out_features` is the
+    full width.  A LoRA A parameter of `local` is treated as replicated: its
+    gradient is all-reduced during backward.
+    """
+
+    def __init__(self, local: nn.Module, out_features: int, group=None, granule: int = 16):
+        super().__init__()
+        self.local = local
+        self.group = group
+        self.out_features = out_features
+        self.world, self.rank = _world(group)
+        self.sizes = [b - a for a, b in (shard_range(out_features, self.world, i, granule) for i in range(self.world))]
+        self.lo, self.hi = shard_range(out_features, self.world, self.rank, granule)
+        lora_a = getattr(local, "lora_A", None)
+        if self.world > 1 and isinstance(lora_a, torch.Tensor) and lora_a.requires_grad:
+            lora_a.register_hook(self._sum_over_ranks)
+
+    def _sum_over_ranks(self, g: torch.Tensor) -> torch.Tensor:
+        g = g.contiguous().clone()
+        dist.all_reduce(g, group=self.group)
+        return g
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return self.local(x)
+        if torch.is_grad_enabled() and x.requires_grad:
+            x = _ReduceGradient.apply(x, self.group)
+        y = self.local(x)
+        return _GatherFeatures.apply(y, self.group, self.sizes, self.rank)
+
+    @classmethod
+    def from_linear(cls, linear: nn.Linear, bits: int = 4, double_quant: bool = True, lora_r: int = 0,
+                    lora_alpha: int = 16, lora_dropout: float = 0.0, group=None,
+                    granule: int = 16) -> "ColumnParallelLinear":
+        """Quantizes this rank's rows of `linear` (every rank passes the same
+        full layer) and wraps them, with LoRA adapters when lora_r > 0 (A
+        broadcast from rank 0 so all ranks hold the same replica; B starts at
+        zero as in LoRALinear)."""
+        world, rank = _world(group)
+        lo, hi = shard_range(linear.out_features, world, rank, granule)
+        shard = nn.Linear(linear.in_features, hi - lo, bias=linear.bias is not None,
+                          dtype=linear.weight.dtype, device=linear.weight.device)
+        with torch.no_grad():
+            shard.weight.copy_(linear.weight[lo:hi])
+            if linear.bias is not None:
+                shard.bias.copy_(linear.bias[lo:hi])
+        local: nn.Module = QuantLinear.from_linear(shard, bits=bits)
+        if double_quant and bits == 4:
+            local.enable_double_quant()
+        if lora_r > 0:
+            local = LoRALinear(local, r=lora_r, lora_alpha=lora_alpha, lora_dropout=lora_dropout).to(
+                linear.weight.device)
+            if world > 1:
+                with torch.no_grad():
+                    dist.broadcast(local.lora_A.data, src=dist.get_global_rank(group, 0) if group else 0,
+                                   group=group)
+        return cls(local, linear.out_features, group=group, granule=granule)
