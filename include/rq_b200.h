@@ -178,6 +178,18 @@ RQ_API int rq_linear_forward_noalloc(int wfmt, const void* qweight, const void* 
                       const void* lora_a, const void* lora_b, int r, float scaling,
                       void* y, void* stream);
 
+/* Kernel family the last rq_linear_forward / rq_linear_dx of this thread
+ * ran: RQ_PATH_GEMV (decode, M <= 16), RQ_PATH_GEMM (tcgen05 prefill GEMM),
+ * RQ_PATH_GEMV_SLABS (the GEMV over 16-row slabs), RQ_PATH_SIMT (exact
+ * CUDA-core kernel), RQ_PATH_NONE (nothing launched).  Introspection for
+ * tests and tuning; no counterpart in the reference. */
+#define RQ_PATH_NONE 0
+#define RQ_PATH_GEMV 1
+#define RQ_PATH_GEMM 2
+#define RQ_PATH_GEMV_SLABS 3
+#define RQ_PATH_SIMT 4
+RQ_API int rq_last_path(void);
+
 /* ------------------------------------- reference launcher drop-ins */
 
 /* Same symbol names, argument order and types as the reference's HIP

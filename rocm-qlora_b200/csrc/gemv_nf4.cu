@@ -554,6 +554,13 @@ static int tensor_map(const MapKey& k, CUtensorMap* out) {
   return RQ_OK;
 }
 
+// Tensor map for other kernels of the library (cached like the GEMV's).
+int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64_t* dims, const uint64_t* strides,
+                      const uint32_t* box, CUtensorMap* out) {
+  MapKey k{ptr, type, swz, rank, {dims[0], dims[1], dims[2]}, {strides[0], strides[1]}, {box[0], box[1], box[2]}};
+  return tensor_map(k, out);
+}
+
 struct Nf4Plan {
   int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
   size_t smem;
@@ -708,14 +715,20 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
 
 }  // namespace rq
 
+namespace rq {
+int gemm_take_timeouts(unsigned int* v);  // gemm_tcgen05.cu
+}
+
 extern "C" int rq_take_kernel_timeouts(unsigned int* count) {
-  unsigned int v = 0, zero = 0;
+  unsigned int v = 0, w = 0, zero = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, rq::g_kernel_timeouts, sizeof(v));
   if (e == cudaSuccess) e = cudaMemcpyToSymbol(rq::g_kernel_timeouts, &zero, sizeof(zero));
   if (e != cudaSuccess) {
     rq::set_cuda_error(e);
     return RQ_ERR_CUDA;
   }
-  if (count) *count = v;
+  const int rc = rq::gemm_take_timeouts(&w);
+  if (rc != RQ_OK) return rc;
+  if (count) *count = v + w;
   return RQ_OK;
 }

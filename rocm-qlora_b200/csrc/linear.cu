@@ -21,6 +21,9 @@ int gemm_forward(const LinearArgs& a, const void* tdown, cudaStream_t st);
 int gemm_dx(const LinearArgs& a, const void* gt, cudaStream_t st);
 
 static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+
+static thread_local int t_last_path = RQ_PATH_NONE;
+int last_path() { return t_last_path; }
 constexpr int64_t kLoraSplitMax = 128;
 
 int64_t linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int r) {
@@ -74,6 +77,7 @@ static int gemv_slabs(const LinearArgs& a, const void* t, cudaStream_t st) {
 
 int linear_forward(const LinearArgs& a, cudaStream_t st) {
   WsView v;
+  t_last_path = RQ_PATH_NONE;
   int rc = carve(a, &v);
   if (rc != RQ_OK) return rc;
   if (a.M == 0 || a.w.N == 0) return RQ_OK;
@@ -85,15 +89,24 @@ int linear_forward(const LinearArgs& a, cudaStream_t st) {
   LinearArgs g = a;
   g.M = a.M < 16 ? a.M : 16;
   if (gemv_supported(g)) {
-    if (a.M <= 16) return gemv_forward(a, v.t, st);
-    if (gemm_supported(a, false)) return gemm_forward(a, v.t, st);
+    if (a.M <= 16) {
+      t_last_path = RQ_PATH_GEMV;
+      return gemv_forward(a, v.t, st);
+    }
+    if (gemm_supported(a, false)) {
+      t_last_path = RQ_PATH_GEMM;
+      return gemm_forward(a, v.t, st);
+    }
+    t_last_path = RQ_PATH_GEMV_SLABS;
     return gemv_slabs(a, v.t, st);
   }
+  t_last_path = RQ_PATH_SIMT;
   return simt_forward(a, v.t, st);
 }
 
 int linear_dx(const LinearArgs& a, cudaStream_t st) {
   WsView v;
+  t_last_path = RQ_PATH_NONE;
   int rc = carve(a, &v);
   if (rc != RQ_OK) return rc;
   if (a.M == 0 || a.w.K == 0) return RQ_OK;
@@ -103,7 +116,11 @@ int linear_dx(const LinearArgs& a, cudaStream_t st) {
                    v.counters, 64, st);
     if (rc != RQ_OK) return rc;
   }
-  if (gemm_supported(a, true)) return gemm_dx(a, v.t, st);
+  if (gemm_supported(a, true)) {
+    t_last_path = RQ_PATH_GEMM;
+    return gemm_dx(a, v.t, st);
+  }
+  t_last_path = RQ_PATH_SIMT;
   return simt_dx(a, v.t, st);
 }
 

@@ -9,6 +9,9 @@
 
 namespace rq {
 
+// Kernel family of the last layer call in this thread (RQ_PATH_*).
+int last_path();
+
 // Records the CUDA error of the last failing launch in this thread.
 void set_cuda_error(cudaError_t e);
 

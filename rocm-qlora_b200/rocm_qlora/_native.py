@@ -48,6 +48,7 @@ def _bind(L: ctypes.CDLL) -> None:
         "rq_status_string": ([I], ctypes.c_char_p),
         "rq_last_cuda_error": ([], I),
         "rq_last_status": ([], I),
+        "rq_last_path": ([], I),
         "rq_take_kernel_timeouts": ([P], I),
         "rq_nf4_quantize": ([P, I, I64, I, P, P, P], I),
         "rq_nf4_dequantize": ([P, I64, P, I, I, P, I, P], I),
@@ -71,7 +72,8 @@ def _bind(L: ctypes.CDLL) -> None:
 
 def exported_symbols() -> Tuple[str, ...]:
     """Names of the C entry points this binding declares."""
-    return ("rq_abi_version", "rq_status_string", "rq_last_cuda_error", "rq_last_status", "rq_take_kernel_timeouts",
+    return ("rq_abi_version", "rq_status_string", "rq_last_cuda_error", "rq_last_status", "rq_last_path",
+            "rq_take_kernel_timeouts",
             "rq_nf4_quantize", "rq_nf4_dequantize", "rq_int8_quantize", "rq_int8_quantize_rows",
             "rq_int8_dequantize", "rq_dq_quantize_scales", "rq_dq_dequantize",
             "rq_linear_workspace_bytes", "rq_linear_forward", "rq_linear_dx", "rq_linear_forward_noalloc",
