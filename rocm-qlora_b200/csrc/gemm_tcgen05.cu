@@ -10,7 +10,7 @@
 // step is one quant block, so a stage needs one scale per weight row.  dX:
 // the step covers 64 weight rows and the tile 256 columns (4 blocks a row);
 // the dequant warps write W transposed (k-major rows of n).  One CTA per
-// SM, 6 warps:
+// SM, 10 warps:
 //   warp 0   TMA producer: X (dY) tile [128 x 64] per stage (128-byte
 //            swizzle), and once the LoRA tiles: forward t = x.A^T [128 x r]
 //            and B [256 x r] (r <= 64, zero-filled to 64 by the TMA bounds);
@@ -21,13 +21,14 @@
 //            shared memory (K-major, 128-byte swizzle); the LoRA product
 //            t . B^T (gt . A) goes to its own accumulator (columns 256..511)
 //            so the epilogue keeps the reference's rounding sequence;
-//   warps 2-5  dequantize the W tile of each stage into shared memory as
+//   warps 2-9  dequantize the W tile of each stage into shared memory as
 //            the reference's exact bf16/f16(T[code] * scale) values, in the
 //            swizzled K-major layout the MMA reads, then run the epilogue:
 //            tcgen05.ld of both accumulators (warp w reads lanes
-//            32*(w%4)...), bias and LoRA rounding, Y stores.
+//            32*(w%4)..., warps w and w+4 split the columns), bias and LoRA
+//            rounding, Y stores.
 // Stages move through mbarriers: X landed (TMA transaction bytes), W tile
-// written (4 dequant-warp arrivals after a proxy fence), slot free
+// written (8 dequant-warp arrivals after a proxy fence), slot free
 // (tcgen05.commit of the MMAs that read it).  Every wait is bounded; a wait
 // that runs out raises the CTA's abort flag, the CTA drains its in-flight
 // copies and MMAs (bounded), frees its tensor memory, skips Y and counts
@@ -66,7 +67,8 @@ namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int kStages = 3;
-constexpr int kThreads = 192;
+constexpr int kDqWarps = 8;                 // dequant / epilogue warps
+constexpr int kThreads = 64 + kDqWarps * 32;
 constexpr uint32_t kABytes = BM * BK * 2;   // 16 KB
 constexpr uint32_t kBBytes = BN * BK * 2;   // 32 KB
 constexpr uint32_t kWaitLimit = 1u << 22;
@@ -89,8 +91,10 @@ constexpr uint32_t kSmA = 0;                               // kStages x 16 KB
 constexpr uint32_t kSmB = kSmA + kStages * kABytes;        // kStages x 32 KB
 constexpr uint32_t kSmT = kSmB + kStages * kBBytes;        // LoRA t tile, 16 KB
 constexpr uint32_t kSmLB = kSmT + kABytes;                 // LoRA B tile, 32 KB
-constexpr uint32_t kSmLut = kSmLB + kBBytes;               // 16 fp32 NF4 levels + 256 fp32 second-level
-constexpr uint32_t kSmBytes = kSmLut + (16 + 256) * 4 + 1024;  // + alignment slack
+constexpr int kLutReps = 16;                               // copies of the code-byte table (one per half-warp lane)
+constexpr uint32_t kSmLut = kSmLB + kBBytes;               // code byte -> (T[lo], T[hi]), 8 copies interleaved
+constexpr uint32_t kSmScl = kSmLut + 256 * kLutReps * 8;   // 256 fp32 second-level values
+constexpr uint32_t kSmBytes = kSmScl + 256 * 4 + 1024;     // + alignment slack
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -190,9 +194,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// two fp32 values rounded to the 16-bit type DT (one packed convert)
 template <int DT>
 __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
-  return pack2<DT>(lo, hi);
+  if constexpr (DT == RQ_BF16) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
 }
 
 template <int DT, bool DX>
@@ -220,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(fullA0 + 8 * i, 1);
-      mbar_init(fullB0 + 8 * i, 4);
+      mbar_init(fullB0 + 8 * i, kDqWarps);
       mbar_init(empty0 + 8 * i, 1);
     }
     mbar_init(lorabar, 1);
@@ -237,10 +248,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // NF4 levels and the second-level table
-  float* lvl = reinterpret_cast<float*>(sm + kSmLut);
-  float* sclut = lvl + 16;
-  if (tid < 16) lvl[tid] = kNF4[tid];
+  // code byte v -> (T[v & 15], T[v >> 4]) in kLutReps interleaved copies
+  // (entry v, copy c at (v * kLutReps + c) * 8: lane l reads copy l % 16, so
+  // the 16 lanes of a half warp hit 16 distinct bank pairs), and the
+  // second-level table
+  float2* lutp = reinterpret_cast<float2*>(sm + kSmLut);
+  float* sclut = reinterpret_cast<float*>(sm + kSmScl);
+  for (int i = tid; i < 256 * kLutReps; i += kThreads) {
+    const int v = i / kLutReps;
+    lutp[i] = make_float2(kNF4[v & 15], kNF4[v >> 4]);
+  }
   if (g.w.fmt != RQ_W_NF4)
     for (int v = tid; v < 256; v += kThreads)
       sclut[v] = g.w.fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(v) : ieee_div((float)(int8_t)v, 127.0f);
@@ -302,83 +319,109 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
       mma_commit(accbar);  // every MMA issued so far is complete
     }
   } else {
-    // ------------------------------------------------ dequant warps (2..5)
-    const int dt = tid - 64;  // 0..127: rows dt and dt + 128 of the W tile
+    // ------------------------------------------------ dequant warps (2..9)
+    // Thread dt owns, per stage: forward tile row dt (weight row n0 + dt,
+    // block kb); dX the 32 codes [32 hf, 32 hf + 32) of block n0/64 + qb4 of
+    // weight rows 64 kb + 2p and +1 (p = dt % 32, qb4 = dt / 64, hf = dt / 32
+    // % 2: a warp's 32 lanes then write one shared row's 32 distinct words).
+    // Raw codes and scales are loaded two stages ahead.
+    const int dt = tid - 64;
     const int fmt = g.w.fmt;
     const int nbk = K / 64;
     const uint8_t* qb = static_cast<const uint8_t*>(g.w.q);
-    for (int kb = 0; kb < nkb; ++kb) {
+    const int p = dt & 31, qb4 = dt >> 6, hf = (dt >> 5) & 1;
+    const uint32_t lut_lane = smem_u32(lutp) + (uint32_t)(lane & (kLutReps - 1)) * 8;
+    // (T[lo], T[hi]) of byte J of `w`: one byte permute, one multiply-add, one 8-byte load
+    auto lut_at = [&](uint32_t w, int j) -> float2 {
+      const uint32_t addr = __byte_perm(w, 0u, 0x4440u | (uint32_t)j) * (kLutReps * 8) + lut_lane;
+      float2 v;
+      asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+      return v;
+    };
+    struct Raw {
+      uint4 c[2];  // forward: 32 code bytes of the row; dX: 16 bytes of each of the two rows
+      uint32_t c2b[2];
+      float sraw[2];
+    };
+    auto fetch = [&](int kb, Raw& r) {
+      r.c[0] = r.c[1] = make_uint4(0u, 0u, 0u, 0u);
+      r.c2b[0] = r.c2b[1] = 0u;
+      r.sraw[0] = r.sraw[1] = 0.0f;
+      if (kb >= nkb) return;
+#pragma unroll
+      for (int h = 0; h < (DX ? 2 : 1); ++h) {
+        const int n = DX ? kb * 64 + 2 * p + h : n0 + dt;
+        const int blk = DX ? (n0 >> 6) + qb4 : kb;
+        if (DX ? blk < nbk : n < N) {
+          const uint4* src = reinterpret_cast<const uint4*>(qb + (size_t)n * (K / 2) + (size_t)blk * 32);
+          if (DX) {
+            r.c[h] = __ldg(src + hf);
+          } else {
+            r.c[0] = __ldg(src);
+            r.c[1] = __ldg(src + 1);
+          }
+          const int64_t bi = (int64_t)n * nbk + blk;
+          if (fmt == RQ_W_NF4) {
+            r.sraw[h] = load_scalar(g.w.scales, g.w.sdt, bi);
+          } else {
+            r.c2b[h] = __ldg(g.w.c2 + bi);
+            r.sraw[h] = __ldg(g.w.c2s + bi / kDQBlock2);
+          }
+        }
+      }
+    };
+    auto convert = [&](int kb, const Raw& r) -> bool {
       const int slot = kb % kStages;
-      if (kb >= kStages && !mbar_wait(empty0 + 8 * slot, ((kb / kStages) - 1) & 1, abortp)) break;
+      float sv[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) sv[h] = fmt == RQ_W_NF4 ? r.sraw[h] : sclut[r.c2b[h]] * r.sraw[h];
+      if (kb >= kStages && !mbar_wait(empty0 + 8 * slot, ((kb / kStages) - 1) & 1, abortp)) return false;
       unsigned char* bt = sm + kSmB + slot * kBBytes;
       if (DX) {
-        // rows n = 64 kb + 2p, +1 and the 64 columns of block q of the
-        // tile: pair p = dt % 32, q = dt / 32 (a warp's 32 lanes write one
-        // shared row's 32 distinct words); tile row k (= output column),
-        // 16-bit pair (n, n+1) at column 2p
-        const int p = dt & 31, q = dt >> 5;
-        const int n = kb * 64 + 2 * p;
-        const int blk = (n0 >> 6) + q;  // 64-block of the weight row
-        uint32_t cw[2][8];
-        float sv[2] = {0.0f, 0.0f};
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) cw[h][i] = 0u;
-          if (blk < nbk) {
-            const uint4* src = reinterpret_cast<const uint4*>(qb + (size_t)(n + h) * (K / 2) + (size_t)blk * 32);
-            const uint4 a0 = __ldg(src), a1 = __ldg(src + 1);
-            cw[h][0] = a0.x, cw[h][1] = a0.y, cw[h][2] = a0.z, cw[h][3] = a0.w;
-            cw[h][4] = a1.x, cw[h][5] = a1.y, cw[h][6] = a1.z, cw[h][7] = a1.w;
-            const int64_t bi = (int64_t)(n + h) * nbk + blk;
-            sv[h] = fmt == RQ_W_NF4 ? load_scalar(g.w.scales, g.w.sdt, bi) : sclut[g.w.c2[bi]] * g.w.c2s[bi / kDQBlock2];
-          }
-        }
+        // tile row k (= output column), 16-bit pair (n, n+1) at column 2p
         const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
+        const uint32_t w0[4] = {r.c[0].x, r.c[0].y, r.c[0].z, r.c[0].w};
+        const uint32_t w1[4] = {r.c[1].x, r.c[1].y, r.c[1].z, r.c[1].w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t b0 = (cw[0][i] >> (8 * j)) & 0xFFu, b1 = (cw[1][i] >> (8 * j)) & 0xFFu;
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int kr = q * 64 + i * 8 + j * 2 + e;  // tile row
-              const float w0 = lvl[e ? (b0 >> 4) : (b0 & 15)] * sv[0], w1 = lvl[e ? (b1 >> 4) : (b1 & 15)] * sv[1];
-              *reinterpret_cast<uint32_t*>(bt + (kr >> 3) * 1024 + (kr & 7) * 128 + ((colb ^ (kr & 7)) << 4) + colo) =
-                  pack_rn<DT>(w0, w1);
-            }
+            const float2 l0 = lut_at(w0[i], j), l1 = lut_at(w1[i], j);
+            const int kr = qb4 * 64 + hf * 32 + i * 8 + j * 2;  // tile rows kr (low nibbles), kr + 1 (high)
+            unsigned char* r0 = bt + (kr >> 3) * 1024 + (kr & 7) * 128 + colo;
+            unsigned char* r1 = bt + ((kr + 1) >> 3) * 1024 + ((kr + 1) & 7) * 128 + colo;
+            *reinterpret_cast<uint32_t*>(r0 + ((colb ^ (kr & 7)) << 4)) = pack_rn<DT>(l0.x * sv[0], l1.x * sv[1]);
+            *reinterpret_cast<uint32_t*>(r1 + ((colb ^ ((kr + 1) & 7)) << 4)) = pack_rn<DT>(l0.y * sv[0], l1.y * sv[1]);
           }
-      } else
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int rr = dt + 128 * h;  // tile row
-        const int n = n0 + rr;
-        uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
-        float s = 0.0f;
-        if (n < N) {
-          const uint4* src = reinterpret_cast<const uint4*>(qb + (size_t)n * (K / 2) + (size_t)kb * 32);
-          c0 = __ldg(src);
-          c1 = __ldg(src + 1);
-          const int64_t bi = (int64_t)n * nbk + kb;
-          s = fmt == RQ_W_NF4 ? load_scalar(g.w.scales, g.w.sdt, bi) : sclut[g.w.c2[bi]] * g.w.c2s[bi / kDQBlock2];
-        }
-        const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      } else {
         // 8 chunks of 16 bytes (8 elements) a row; chunk c at (c ^ (row & 7))
-        unsigned char* rowp = bt + (rr >> 3) * 1024 + (rr & 7) * 128;
+        const uint32_t cw[8] = {r.c[0].x, r.c[0].y, r.c[0].z, r.c[0].w, r.c[1].x, r.c[1].y, r.c[1].z, r.c[1].w};
+        unsigned char* rowp = bt + (dt >> 3) * 1024 + (dt & 7) * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          uint32_t q[4];
+          uint32_t qv[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t byte = (cw[c] >> (8 * j)) & 0xFFu;
-            q[j] = pack_rn<DT>(lvl[byte & 15] * s, lvl[byte >> 4] * s);
+            const float2 l = lut_at(cw[c], j);
+            qv[j] = pack_rn<DT>(l.x * sv[0], l.y * sv[0]);
           }
-          *reinterpret_cast<uint4*>(rowp + ((c ^ (rr & 7)) << 4)) = make_uint4(q[0], q[1], q[2], q[3]);
+          *reinterpret_cast<uint4*>(rowp + ((c ^ (dt & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
       __syncwarp();
       if (lane == 0) mbar_arrive(fullB0 + 8 * slot);
+      return true;
+    };
+    Raw ra, rb;
+    fetch(0, ra);
+    fetch(1, rb);
+    for (int kb = 0; kb < nkb; kb += 2) {
+      if (!convert(kb, ra)) break;
+      fetch(kb + 2, ra);
+      if (kb + 1 >= nkb) break;
+      if (!convert(kb + 1, rb)) break;
+      fetch(kb + 3, rb);
     }
 
     // ---------------------------------------------------------- epilogue
@@ -386,9 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int quad = warp & 3;  // tensor-memory lanes 32*quad ... are this warp's rows
     const int row = quad * 32 + lane, m = m0 + row;
+    const int c_lo = ((warp - 2) >> 2) * (BN / 2);  // warps w and w+4 split the columns
     const bool has_bias = !DX && g.bias != nullptr;
     T* y = static_cast<T*>(g.y);
-    for (int cb = 0; cb < BN; cb += 32) {
+    for (int cb = c_lo; cb < c_lo + BN / 2; cb += 32) {
       float acc[32], u[32];
       tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + cb, acc);
       if (has_lora) tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + 256 + cb, u);

@@ -292,6 +292,98 @@ static int lora_small_launch(const void* X, int M, int Kr, const void* W2, int R
 }
 
 // fp32 activations: one thread per output, CUDA cores.
+// M > 16: one CTA of kWideWarps warps per 16 rows of X.  The warps split
+// the reduction dimension into contiguous chunks (16-aligned), each
+// loading the next k-step's fragments while it multiplies the current one,
+// and meet in shared memory in a fixed order (deterministic, no workspace).
+constexpr int kWideWarps = 8;
+
+template <int DT, bool WT, int NT>
+__global__ void __launch_bounds__(kWideWarps * 32) lora_down_wide_k(const typename DType<DT>::T* __restrict__ X,
+                                                                     int64_t M, int64_t Kr,
+                                                                     const typename DType<DT>::T* __restrict__ W2,
+                                                                     int R, float pre_s, int do_pre,
+                                                                     typename DType<DT>::T* __restrict__ out) {
+  using T = typename DType<DT>::T;
+  constexpr int RP = NT * 8 + 4;  // padded row of the partials
+  __shared__ float part[kWideWarps][16][RP];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t m0 = (int64_t)blockIdx.x * 16;
+  const int64_t steps = (Kr + 15) / 16;
+  const int64_t s0 = steps * warp / kWideWarps, s1 = steps * (warp + 1) / kWideWarps;
+  const bool vec_x = ((uintptr_t)X % 4 == 0) && (Kr % 2 == 0);
+  const bool vec_w = ((uintptr_t)W2 % 4 == 0) && (Kr % 2 == 0);
+  const int64_t ra = m0 + g, rb = m0 + g + 8;
+  const T* xa = X + (ra < M ? ra : 0) * Kr;
+  const T* xb = X + (rb < M ? rb : 0) * Kr;
+  float acc[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+  auto load = [&](int64_t st, uint32_t (&a)[4], uint32_t (&b)[NT][2]) {
+    const int64_t k0 = st * 16;
+    a[0] = ra < M ? ld_pair<DT>(xa, k0 + 2 * t, Kr, vec_x) : 0u;
+    a[1] = rb < M ? ld_pair<DT>(xb, k0 + 2 * t, Kr, vec_x) : 0u;
+    a[2] = ra < M ? ld_pair<DT>(xa, k0 + 8 + 2 * t, Kr, vec_x) : 0u;
+    a[3] = rb < M ? ld_pair<DT>(xb, k0 + 8 + 2 * t, Kr, vec_x) : 0u;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = nt * 8 + g;
+      uint32_t b0 = 0, b1 = 0;
+      if (n < R) {
+        if (!WT) {
+          b0 = ld_pair<DT>(W2 + (int64_t)n * Kr, k0 + 2 * t, Kr, vec_w);
+          b1 = ld_pair<DT>(W2 + (int64_t)n * Kr, k0 + 8 + 2 * t, Kr, vec_w);
+        } else {
+          const int64_t ka = k0 + 2 * t, kb = k0 + 8 + 2 * t;
+          const uint32_t e0 = ka < Kr ? bits16<DT>(W2[ka * R + n]) : 0u;
+          const uint32_t e1 = ka + 1 < Kr ? bits16<DT>(W2[(ka + 1) * R + n]) : 0u;
+          const uint32_t e2 = kb < Kr ? bits16<DT>(W2[kb * R + n]) : 0u;
+          const uint32_t e3 = kb + 1 < Kr ? bits16<DT>(W2[(kb + 1) * R + n]) : 0u;
+          b0 = e0 | (e1 << 16);
+          b1 = e2 | (e3 << 16);
+        }
+      }
+      b[nt][0] = b0;
+      b[nt][1] = b1;
+    }
+  };
+  uint32_t a[2][4], b[2][NT][2];
+  if (s0 < s1) load(s0, a[0], b[0]);
+  for (int64_t st = s0; st < s1; st += 2) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (st + h < s1) {
+        if (st + h + 1 < s1) load(st + h + 1, a[h ^ 1], b[h ^ 1]);
+        uint32_t av[4] = {a[h][0], a[h][1], a[h][2], a[h][3]};
+        if (do_pre) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) av[i] = prescale_pair<DT>(av[i], pre_s);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) MmaOp<DT>::mma(acc[nt], av, b[h][nt][0], b[h][nt][1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int c = nt * 8 + 2 * t;
+    part[warp][g][c] = acc[nt][0];
+    part[warp][g][c + 1] = acc[nt][1];
+    part[warp][g + 8][c] = acc[nt][2];
+    part[warp][g + 8][c + 1] = acc[nt][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * R; i += blockDim.x) {
+    const int rr = i / R, c = i - rr * R;
+    const int64_t m = m0 + rr;
+    if (m >= M) continue;
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWideWarps; ++w) v += part[w][rr][c];
+    out[m * R + c] = DType<DT>::from_f32(v);
+  }
+}
+
 template <bool WT>
 __global__ void __launch_bounds__(256) lora_down_f32_k(const float* __restrict__ X, int64_t M, int64_t Kr,
                                                        const float* __restrict__ W2, int R, float pre_s, int do_pre,
@@ -332,10 +424,18 @@ static int lora_down_t(const void* X, int64_t M, int64_t Kr, const void* W2, int
     lora_down_mma_k<DT, WT, 1><<<dim3(1, (unsigned)ksplit), 32, 0, st>>>(
         (const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (int)kchunk, partial, counters, (T*)out);
   } else {
-    const int64_t tiles = (M + 63) / 64;
+    const int64_t tiles = (M + 15) / 16;
     if (tiles > 0x7fffffff) return RQ_ERR_INVALID;
-    lora_down_mma_k<DT, WT, 4><<<dim3((unsigned)tiles, 1), 128, 0, st>>>(
-        (const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (int)Kr, partial, counters, (T*)out);
+    const dim3 grid((unsigned)tiles);
+    if (R <= 16)
+      lora_down_wide_k<DT, WT, 2><<<grid, kWideWarps * 32, 0, st>>>((const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (T*)out);
+    else if (R <= 32)
+      lora_down_wide_k<DT, WT, 4><<<grid, kWideWarps * 32, 0, st>>>((const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (T*)out);
+    else if (R <= 64)
+      lora_down_wide_k<DT, WT, 8><<<grid, kWideWarps * 32, 0, st>>>((const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (T*)out);
+    else  // r in (64, 128]: 4-warp CTAs over 64 rows, each warp the whole reduction
+      lora_down_mma_k<DT, WT, 4><<<dim3((unsigned)((M + 63) / 64), 1), 128, 0, st>>>(
+          (const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (int)Kr, partial, counters, (T*)out);
   }
   return check_launch();
 }
