@@ -175,14 +175,17 @@ def run_ours(args, rank, world, device):
                 gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
 
     def step(c, lora=True):
+        """One sweep pass.  lora=True is the measured step (adapter, and the
+        all-gather of Y when sharded); lora=False is the roofline leg: the
+        dequant GEMV kernels alone, no adapter and no collective."""
         for si, M in calls:
             w = wsets[c][si]
             if lora:
                 y = layer_ops.forward(w, xs[(si, M)], None, A[si], B[si], ALPHA / R)
+                if world > 1:
+                    dist.all_gather_into_tensor(gather_out[(si, M)], y)
             else:
-                y = layer_ops.forward(w, xs[(si, M)], None, None, None, 1.0)
-            if world > 1:
-                dist.all_gather_into_tensor(gather_out[(si, M)], y)
+                layer_ops.forward(w, xs[(si, M)], None, None, None, 1.0)
 
     def capture(lora):
         graphs = []
@@ -229,13 +232,24 @@ def run_ours(args, rank, world, device):
             dist.barrier()
         return ms
 
+    def all_done(flag: bool) -> bool:
+        """True once any rank is done: every rank then takes the same number
+        of load batches (each replay holds collectives when world > 1)."""
+        if world == 1:
+            return flag
+        t = torch.tensor([1 if flag else 0], device=device, dtype=torch.int32)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return bool(t.item())
+
     run_steps(args.warmup, 0, True, graphs)
     with ClockSampler(device.index) as clk:
         # untimed load for the sampler (about 0.4 s), then the timed steps
         t_end = time.perf_counter() + 0.4
-        while time.perf_counter() < t_end:
+        done = False
+        while not done:
             run_steps(50, 0, True, graphs)
             torch.cuda.synchronize(device)
+            done = all_done(time.perf_counter() >= t_end)
         ms = timed(args.steps, True, graphs)
     clocks = clk.summary()
     step_bytes = sum(algo_bytes(SHAPES[si][0], SHAPES[si][1], M, R) for si, M in calls)
@@ -265,6 +279,8 @@ def run_ours(args, rank, world, device):
 
     # CPU baseline on rank 0 (bounded sample of the same workload)
     cpu = cpu_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    # configs[2] (prefill / training GEMM), single GPU
+    prefill = prefill_leg(device) if (world == 1 and not args.no_prefill) else None
 
     if rank == 0:
         line = {
@@ -285,8 +301,75 @@ def run_ours(args, rank, world, device):
             "e2e": e2e,
             "gpu_launches": args.steps * len(calls) * 2,
             "clocks": clocks,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
+
+
+PREFILL_MS = [512, 2048, 8192]
+PREFILL_R, PREFILL_ALPHA = 64, 128
+
+
+def prefill_leg(device, iters=5):
+    """the tcgen05 dequant GEMM on the three 7B shapes at
+    M in {512, 2048, 8192}, forward Y and backward dX, LoRA r=64 alpha=128,
+    timed with CUDA events (mean of `iters` calls after 2 warm-up calls).
+    FLOPs per call: 2MNK + 2Mr(K+N)."""
+    import torch.nn as nn
+    from rocm_qlora import LoRALinear, QuantLinear
+    from rocm_qlora.quantization import layer_ops
+    from tests.inputs import layer_inputs
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        peak = float(pk.get("bf16_tflops_sustained") or pk["bf16_tflops"])
+    except Exception:
+        peak = 1400.0
+    out = {"fwd": {}, "dx": {}}
+    flops_all, t_all = 0.0, 0.0
+    for si, (N, K) in enumerate(SHAPES):
+        inp = layer_inputs(N, K, 1, sigma=0.02, r=PREFILL_R, alpha=PREFILL_ALPHA, seed=200 + si)
+        lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=device)
+        with torch.no_grad():
+            lin.weight.copy_(inp.W.to(device))
+        ql = QuantLinear.from_linear(lin, bits=4)
+        ql.enable_double_quant()
+        lora = LoRALinear(ql, r=PREFILL_R, lora_alpha=PREFILL_ALPHA).to(device).eval()
+        with torch.no_grad():
+            lora.lora_A.copy_(inp.A)
+            lora.lora_B.copy_(inp.B)
+        w = ql.weight_view()
+        A = lora.lora_A.detach().bfloat16().contiguous()
+        B = lora.lora_B.detach().bfloat16().contiguous()
+        g = torch.Generator(device=device).manual_seed(si)
+        for M in PREFILL_MS:
+            x = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16)
+            dy = torch.randn(M, N, generator=g, device=device).to(torch.bfloat16)
+            fl = 2.0 * M * N * K + 2.0 * M * PREFILL_R * (K + N)
+            for kind, fn in (("fwd", lambda: layer_ops.forward(w, x, None, A, B, lora.scaling)),
+                             ("dx", lambda: layer_ops.dx(w, dy, A, B, lora.scaling))):
+                for _ in range(2):
+                    fn()
+                torch.cuda.synchronize(device)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize(device)
+                us = e0.elapsed_time(e1) * 1e3 / iters
+                out[kind][f"{N}x{K}/M{M}"] = round(fl / us / 1e6, 1)
+                flops_all += fl
+                t_all += us
+            del x, dy
+        del lora, ql, lin
+    tf = flops_all / t_all / 1e6
+    return {"metric": "prefill TFLOP/s (2MNK + 2Mr(K+N) per call, incl. the LoRA down product)",
+            "unit": "TFLOP/s", "value": round(tf, 1), "peak": peak,
+            "peak_kind": "measured sustained" if peak != 1400.0 else "fallback", "frac": round(tf / peak, 4),
+            "config": "configs[2]: 7B shapes x M in {512,2048,8192}, forward and dX, NF4 double quant, r64 a128",
+            "per_call_tflops": out}
 
 
 def rotated_modules(layers, wsets):
@@ -334,11 +417,18 @@ def run_e2e(args, mods, device, world):
         one(i)
     torch.cuda.synchronize(device)
     dt = time.perf_counter() - t0
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([dt], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
     step_bytes = sum(algo_bytes(SHAPES[si][0], SHAPES[si][1], M, R) for si, M in calls)
     h2d = sum(M * SHAPES[si][1] * 2 for si, M in calls)
     d2h = sum(M * SHAPES[si][0] * 2 for si, M in calls)
-    return {"value": round(step_bytes * args.steps / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "note": "eager LoRALinear.forward per call, wall clock, no CUDA graph"}
+    return {"value": round(step_bytes * args.steps * world / dt / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "note": "eager LoRALinear.forward per call (each rank its shard), wall clock max over ranks, "
+                    "no CUDA graph"}
 
 
 # --------------------------------------------------------- CPU reference
@@ -484,6 +574,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill GEMM leg")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
