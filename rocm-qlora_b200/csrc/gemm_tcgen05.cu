@@ -1,45 +1,56 @@
 // gemm_tcgen05.cu -- prefill/training-shaped fused NF4 dequant GEMM on the
-// 5th-generation tensor cores (tcgen05, accumulators in tensor memory).
+// 5th-generation tensor cores (tcgen05, accumulators in tensor memory),
+// issued as 2-SM MMAs by CTA pairs.
 //
 // Forward  Y[M, N]  = X[M, K] . deq(W[N, K])^T (+ bias, + LoRA), and the
 // transposed variant for backward  dX[M, K] = dY[M, N] . deq(W) (+ LoRA),
 // for M >= 64, bf16/f16 activations, NF4 weights (plain, fp8 or int8
 // double-quantized scales).
 //
-// CTA tile 128 (tokens) x 256 (outputs), reduction step 64.  Forward: the
-// step is one quant block, so a stage needs one scale per weight row.  dX:
-// the step covers 64 weight rows and the tile 256 columns (4 blocks a row);
-// the dequant warps write W transposed (k-major rows of n).  One CTA per
-// SM, 10 warps:
-//   warp 0   TMA producer: X (dY) tile [128 x 64] per stage (128-byte
-//            swizzle), and once the LoRA tiles: forward t = x.A^T [128 x r]
-//            and B [256 x r] (r <= 64, zero-filled to 64 by the TMA bounds);
-//            dX gt = rnd(dY*s).B [128 x r] and A [r x 256] (read as an
-//            MN-major operand: four 64-column boxes);
-//   warp 1   allocates 512 tensor-memory columns; lane 0 issues the MMAs:
-//            tcgen05.mma kind::f16, M=128 N=256 K=16, both operands from
-//            shared memory (K-major, 128-byte swizzle); the LoRA product
-//            t . B^T (gt . A) goes to its own accumulator (columns 256..511)
-//            so the epilogue keeps the reference's rounding sequence;
-//   warps 2-9  dequantize the W tile of each stage into shared memory as
-//            the reference's exact bf16/f16(T[code] * scale) values, in the
-//            swizzled K-major layout the MMA reads, then run the epilogue:
-//            tcgen05.ld of both accumulators (warp w reads lanes
-//            32*(w%4)..., warps w and w+4 split the columns), bias and LoRA
-//            rounding, Y stores.
-// Stages move through mbarriers: X landed (TMA transaction bytes), W tile
-// written (8 dequant-warp arrivals after a proxy fence), slot free
-// (tcgen05.commit of the MMAs that read it).  Every wait is bounded; a wait
-// that runs out raises the CTA's abort flag, the CTA drains its in-flight
-// copies and MMAs (bounded), frees its tensor memory, skips Y and counts
-// in the kernel-timeout counter.
+// A cluster of two CTAs (one per SM) computes a 256 (tokens) x BN (outputs)
+// tile, BN = 256 or 128, with tcgen05.mma.cta_group::2 (M = 256): each CTA
+// holds its 128 token rows of the activation tile and HALF of the weight
+// tile (BN/2 outputs), and the pair's two tensor cores share both.  The
+// dequantized weight is the expensive operand to produce, so each SM
+// dequantizes half of what a one-SM 128 x BN tile would need per FLOP.
+// The reduction step is 64 (one quant block a weight row in the forward;
+// dX steps over 64 weight rows and writes the tile transposed).
+// 10 warps a CTA:
+//   warp 0   TMA producer of this CTA's activation tile [128 x 64] per
+//            stage (128-byte swizzle) and, once, its LoRA tiles: forward
+//            t = x.A^T [128 x r] and B [BN/2 x r] (r <= 64, zero-filled to 64
+//            by the TMA bounds); dX gt = rnd(dY*s).B [128 x r] and A [r x BN/2]
+//            (an MN-major operand of 64-column boxes);
+//   warp 1   allocates the pair's tensor memory (base accumulator columns
+//            0..BN-1, LoRA accumulator BN..2BN-1, so the epilogue keeps the
+//            reference's rounding sequence).  In the leader CTA (rank 0)
+//            lane 0 issues every MMA of the pair (kind::f16, K = 16, both
+//            operands K-major from shared memory, B of the dX LoRA product
+//            MN-major) and commits each stage to the stage-free barriers of
+//            BOTH CTAs (tcgen05.commit multicast); in the peer CTA lane 0
+//            forwards "both of this CTA's tiles of the stage are ready" to the
+//            leader, the one cluster-scope release a stage (a thread with no
+//            loads in flight, so the release costs no wait);
+//   warps 2-9  dequantize this CTA's half of the weight tile of each stage
+//            as the reference's exact bf16/f16(T[code] * scale) values into
+//            the swizzled K-major layout, arrive on their CTA's fullB, then
+//            run the epilogue on this CTA's 128 rows: tcgen05.ld of both
+//            accumulators, bias and LoRA rounding, Y stores.
+// Barriers: fullA (own TMA bytes), fullB (own 8 dequant warps, plus the
+// peer's forward in the leader), empty (MMA commit), lora / lorafwd, acc
+// (final commit, both CTAs).  Grid (2, output tiles, token pairs): the
+// clusters that run together share token rows, so X stays in L2.  Every wait is
+// bounded; a wait that runs out raises the abort flag of both CTAs, each
+// CTA drains what it has in flight (bounded), Y is not written, the pair
+// meets at a cluster barrier before the tensor memory is released, and the
+// kernel-timeout counter records it.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
 #include <vector>
 
-#include "linear_common.cuh"
+#include "gemv_common.cuh"
 #include "rq_internal.h"
 
 namespace rq {
@@ -65,19 +76,41 @@ int gemm_take_timeouts(unsigned int* v) {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kStages = 3;
+constexpr int BM = 128;                     // token rows a CTA (a pair: 256)
+constexpr int BK = 64;
 constexpr int kDqWarps = 8;                 // dequant / epilogue warps
 constexpr int kThreads = 64 + kDqWarps * 32;
 constexpr uint32_t kABytes = BM * BK * 2;   // 16 KB
-constexpr uint32_t kBBytes = BN * BK * 2;   // 32 KB
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr int kTmemCols = 512;              // base accumulator 0..255, LoRA 256..511
+constexpr int kLutReps = 16;                // copies of the code-byte table (one per half-warp lane)
+constexpr uint32_t kLutBytes = 256 * kLutReps * 8;
+constexpr uint32_t kSmemCap = 226 * 1024;   // dynamic shared memory budget (static + margin in the last KB)
+
+// Per-CTA shared-memory plan of a BN-wide pair tile (1 KB aligned offsets)
+template <int BN>
+struct Tile {
+  static constexpr int BNH = BN / 2;                  // weight rows (dX: output columns) a CTA
+  static constexpr uint32_t kBBytes = BNH * BK * 2;   // 16 KB / 8 KB
+  static constexpr uint32_t kStage = kABytes + kBBytes;
+  static constexpr uint32_t kFixed = kABytes + kBBytes + kLutBytes + 1024 + 1024;  // LoRA tiles, LUT, sclut, align
+  static constexpr int kFit = (int)((kSmemCap - kFixed) / kStage);
+  static constexpr int kStages = kFit > 6 ? 6 : kFit;
+  static constexpr uint32_t kSmA = 0;                               // kStages x 16 KB
+  static constexpr uint32_t kSmB = kSmA + kStages * kABytes;        // kStages x kBBytes
+  static constexpr uint32_t kSmT = kSmB + kStages * kBBytes;        // LoRA t (gt) tile, 16 KB
+  static constexpr uint32_t kSmLB = kSmT + kABytes;                 // LoRA B (dX: A) tile
+  static constexpr uint32_t kSmLut = kSmLB + kBBytes;               // code byte -> (T[lo], T[hi])
+  static constexpr uint32_t kSmScl = kSmLut + kLutBytes;            // 256 fp32 second-level values
+  static constexpr uint32_t kSmBytes = kSmScl + 1024 + 1024;        // + alignment slack
+  static constexpr int kTmemCols = 2 * BN;                          // base + LoRA accumulators
+  static_assert(kStages >= 3, "pipeline too shallow");
+  static_assert(kSmBytes <= kSmemCap, "shared memory plan too large");
+};
 
 struct GemmArgs {
   CUtensorMap xmap;   // X [M][K] (dX: dY [M][N]), box 64 x 128, 128-byte swizzle
   CUtensorMap tmap;   // t [M][r] (dX: gt), box 64 x 128, 128-byte swizzle (r < 64 zero-filled)
-  CUtensorMap bmap;   // LoRA B [N][r], box 64 x 256 (dX: A [r][K], box 64 x 64), 128-byte swizzle
+  CUtensorMap bmap;   // LoRA B [N][r], box 64 x BN/2 (dX: A [r][K], box 64 x 64), 128-byte swizzle
   QWeight w;
   const void* bias;
   int bdt;
@@ -86,45 +119,86 @@ struct GemmArgs {
   float s;            // LoRA scaling (dX: 1, gt already carries it)
 };
 
-// dynamic shared memory layout (1 KB aligned base)
-constexpr uint32_t kSmA = 0;                               // kStages x 16 KB
-constexpr uint32_t kSmB = kSmA + kStages * kABytes;        // kStages x 32 KB
-constexpr uint32_t kSmT = kSmB + kStages * kBBytes;        // LoRA t tile, 16 KB
-constexpr uint32_t kSmLB = kSmT + kABytes;                 // LoRA B tile, 32 KB
-constexpr int kLutReps = 16;                               // copies of the code-byte table (one per half-warp lane)
-constexpr uint32_t kSmLut = kSmLB + kBBytes;               // code byte -> (T[lo], T[hi]), 8 copies interleaved
-constexpr uint32_t kSmScl = kSmLut + 256 * kLutReps * 8;   // 256 fp32 second-level values
-constexpr uint32_t kSmBytes = kSmScl + 256 * 4 + 1024;     // + alignment slack
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the variable at shared::cta address `a` in CTA `rank`
+__device__ __forceinline__ uint32_t mapa(uint32_t a, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void st_cluster(uint32_t caddr, int v) {
+  asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(caddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// arrive (release at cluster scope) on a barrier given by its shared::cluster address
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+template <bool kCluster>
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
+  if constexpr (kCluster)
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+  else
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_test(bar, parity)) return true;
-    if (*abort_flag) return false;
+
+// The abort state of a CTA pair: this CTA's flag and the peer's (remote).
+struct Abort {
+  volatile int* mine;
+  uint32_t peer;  // shared::cluster address of the peer's flag
+  __device__ __forceinline__ bool raised() const { return *mine != 0; }
+  __device__ __forceinline__ void raise() const {
+    *mine = 1;
+    st_cluster(peer, 1);
   }
-  *abort_flag = 1;
+};
+
+// Bounded wait for the phase of parity `parity`; false if either CTA of the
+// pair gave up (then or earlier).
+template <bool kCluster = false>
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_test<kCluster>(bar, parity)) return true;
+    if (ab.raised()) return false;
+  }
+  ab.raise();
   atomicAdd(&g_gemm_timeouts, 1u);
   return false;
 }
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit && !mbar_test<false>(bar, parity); ++i) {
+  }
+}
+
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -159,23 +233,28 @@ __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo) 
 }
 
 // Instruction descriptor: 16-bit A/B of type DT, fp32 accumulate, A K-major,
-// B K-major (or MN-major), M=128, N=256.
-template <int DT>
-__device__ __forceinline__ uint32_t idesc_f16(bool b_mn = false) {
+// B K-major (or MN-major), M = 256 (the CTA pair), N = BN.
+template <int DT, int BN>
+__device__ __forceinline__ uint32_t idesc_pair(bool b_mn = false) {
   const uint32_t ab = DT == RQ_BF16 ? 1u : 0u;
   return (1u << 4) | (ab << 7) | (ab << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(256 >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
+__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
       "l"(da), "l"(db), "r"(idesc), "r"(accum)
       : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+// Arrive on the barrier at shared::cta offset `bar` of each CTA in `mask`
+// once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
 }
 
 // 32 consecutive fp32 columns of this thread's accumulator row
@@ -206,54 +285,63 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
   }
 }
 
-template <int DT, bool DX>
-__global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ GemmArgs g) {
+template <int DT, bool DX, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ GemmArgs g) {
+  using TL = Tile<BN>;
   using T = typename DType<DT>::T;
+  constexpr int S = TL::kStages, BNH = TL::BNH;
+  constexpr uint32_t kBBytes = TL::kBBytes;
   extern __shared__ __align__(1024) unsigned char dsm[];
-  __shared__ __align__(8) uint64_t bars[3 * kStages + 3];  // fullA[S], fullB[S], empty[S], lora, acc, drain
+  // fullA[S], fullB[S], empty[S], lora, lorafwd, acc, drain
+  __shared__ __align__(8) uint64_t bars[3 * S + 4];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_flag, a_issued, mma_done;
+  __shared__ int abort_flag, a_issued, consumed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // 1 KB aligned view of the dynamic shared memory (swizzle atoms)
+  const uint32_t rank = cluster_rank();  // 0: leader (issues the pair's MMAs), 1: peer
+  // 1 KB aligned view of the dynamic shared memory (swizzle atoms); the
+  // same offsets in both CTAs, which the pair's MMAs rely on
   const uint32_t sraw = smem_u32(dsm);
   const uint32_t sbase = (sraw + 1023u) & ~1023u;
   unsigned char* sm = dsm + (sbase - sraw);
-  const uint32_t fullA0 = smem_u32(bars), fullB0 = fullA0 + 8 * kStages, empty0 = fullB0 + 8 * kStages;
-  const uint32_t lorabar = empty0 + 8 * kStages, accbar = lorabar + 8, drainbar = accbar + 8;
-  volatile int* abortp = &abort_flag;
+  const uint32_t fullA0 = smem_u32(bars), fullB0 = fullA0 + 8 * S, empty0 = fullB0 + 8 * S;
+  const uint32_t lorabar = empty0 + 8 * S, lorafwd = lorabar + 8, accbar = lorafwd + 8, drainbar = accbar + 8;
+  const Abort ab{&abort_flag, mapa(smem_u32(&abort_flag), rank ^ 1u)};
 
   const int M = g.M, N = g.N, K = g.K;
-  const int W_out = DX ? K : N;  // output columns
+  const int W_out = DX ? K : N;       // output columns
   const int nkb = (DX ? N : K) / BK;  // reduction steps
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.y * BN;     // the pair's first output column
+  const int nh0 = n0 + (int)rank * BNH;  // this CTA's half: weight rows (forward) / output columns (dX)
+  const int m0 = (blockIdx.z * 2 + (int)rank) * BM;  // this CTA's token rows
   const bool has_lora = g.r > 0;
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(fullA0 + 8 * i, 1);
-      mbar_init(fullB0 + 8 * i, kDqWarps);
+      mbar_init(fullB0 + 8 * i, rank == 0 ? kDqWarps + 1 : kDqWarps);
       mbar_init(empty0 + 8 * i, 1);
     }
     mbar_init(lorabar, 1);
+    mbar_init(lorafwd, 1);
     mbar_init(accbar, 1);
     mbar_init(drainbar, 1);
     abort_flag = 0;
     a_issued = 0;
-    mma_done = 0;
+    consumed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // whole warp: tensor-memory allocation
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
-                 "r"(kTmemCols)
+  if (warp == 1) {  // whole warp, in both CTAs: the pair's tensor memory
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(TL::kTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   // code byte v -> (T[v & 15], T[v >> 4]) in kLutReps interleaved copies
   // (entry v, copy c at (v * kLutReps + c) * 8: lane l reads copy l % 16, so
   // the 16 lanes of a half warp hit 16 distinct bank pairs), and the
   // second-level table
-  float2* lutp = reinterpret_cast<float2*>(sm + kSmLut);
-  float* sclut = reinterpret_cast<float*>(sm + kSmScl);
+  float2* lutp = reinterpret_cast<float2*>(sm + TL::kSmLut);
+  float* sclut = reinterpret_cast<float*>(sm + TL::kSmScl);
   for (int i = tid; i < 256 * kLutReps; i += kThreads) {
     const int v = i / kLutReps;
     lutp[i] = make_float2(kNF4[v & 15], kNF4[v >> 4]);
@@ -261,75 +349,104 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
   if (g.w.fmt != RQ_W_NF4)
     for (int v = tid; v < 256; v += kThreads)
       sclut[v] = g.w.fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(v) : ieee_div((float)(int8_t)v, 127.0f);
+  // both CTAs' barriers initialised and the tensor memory allocated before
+  // any cross-CTA arrive, commit or MMA
+  __syncwarp();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
+  cluster_sync();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base_sh;
+  const uint32_t fullB_lead = mapa(fullB0, 0);  // the leader's fullB[0] (cluster address)
 
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
     if (lane == 0) {
       if (has_lora) {
         mbar_expect_tx(lorabar, kABytes + kBBytes);
-        tma_2d(sbase + kSmT, &g.tmap, 0, m0, lorabar);
+        tma_2d(sbase + TL::kSmT, &g.tmap, 0, m0, lorabar);
         if (DX) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_2d(sbase + kSmLB + j * 8192, &g.bmap, n0 + 64 * j, 0, lorabar);
+          for (int j = 0; j < BNH / 64; ++j) tma_2d(sbase + TL::kSmLB + j * 8192, &g.bmap, nh0 + 64 * j, 0, lorabar);
         } else {
-          tma_2d(sbase + kSmLB, &g.bmap, 0, n0, lorabar);
+          tma_2d(sbase + TL::kSmLB, &g.bmap, 0, nh0, lorabar);
         }
       }
       for (int kb = 0; kb < nkb; ++kb) {
-        const int slot = kb % kStages;
-        if (kb >= kStages && !mbar_wait(empty0 + 8 * slot, ((kb / kStages) - 1) & 1, abortp)) break;
+        const int slot = kb % S;
+        if (kb >= S && !mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab)) break;
         mbar_expect_tx(fullA0 + 8 * slot, kABytes);
-        tma_2d(sbase + kSmA + slot * kABytes, &g.xmap, kb * BK, m0, fullA0 + 8 * slot);
+        tma_2d(sbase + TL::kSmA + slot * kABytes, &g.xmap, kb * BK, m0, fullA0 + 8 * slot);
         *reinterpret_cast<volatile int*>(&a_issued) = kb + 1;
       }
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16<DT>();
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------- MMA issuer (leader CTA)
+      const uint32_t idesc = idesc_pair<DT, BN>();
       bool ok = true;
       if (has_lora) {
-        ok = mbar_wait(lorabar, 0, abortp);
+        ok = mbar_wait(lorabar, 0, ab) && mbar_wait<true>(lorafwd, 0, ab);
         if (ok) {
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t db = DX ? sw128_mn_desc(sbase + kSmLB + kk * 2048, 8192)  // rows 16kk.. of A
-                                   : sw128_desc(sbase + kSmLB + kk * 32);
-            mma_f16(tmem + 256, sw128_desc(sbase + kSmT + kk * 32), db, DX ? idesc_f16<DT>(true) : idesc, kk > 0);
+            const uint64_t db = DX ? sw128_mn_desc(sbase + TL::kSmLB + kk * 2048, 8192)  // rows 16kk.. of A
+                                   : sw128_desc(sbase + TL::kSmLB + kk * 32);
+            mma_pair(tmem + BN, sw128_desc(sbase + TL::kSmT + kk * 32), db, DX ? idesc_pair<DT, BN>(true) : idesc,
+                     kk > 0);
           }
         }
       }
       for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int slot = kb % kStages;
-        const uint32_t par = (kb / kStages) & 1;
-        if (!mbar_wait(fullA0 + 8 * slot, par, abortp) || !mbar_wait(fullB0 + 8 * slot, par, abortp)) break;
+        const int slot = kb % S;
+        const uint32_t par = (kb / S) & 1;
+        if (!mbar_wait(fullA0 + 8 * slot, par, ab) || !mbar_wait<true>(fullB0 + 8 * slot, par, ab)) {
+          ok = false;
+          break;
+        }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a = sbase + kSmA + slot * kABytes, b = sbase + kSmB + slot * kBBytes;
+        const uint32_t a = sbase + TL::kSmA + slot * kABytes, b = sbase + TL::kSmB + slot * kBBytes;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          mma_f16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(empty0 + 8 * slot);  // the slot is free once these MMAs have read it
-        *reinterpret_cast<volatile int*>(&mma_done) = kb + 1;
+          mma_pair(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit_pair(empty0 + 8 * slot, 3);  // both CTAs' slot is free once these MMAs have read it
+        *reinterpret_cast<volatile int*>(&consumed) = kb + 1;
       }
-      mma_commit(accbar);  // every MMA issued so far is complete
+      if (ok && !ab.raised()) mma_commit_pair(accbar, 3);  // every MMA of the tile is complete
+    } else if (lane == 0) {
+      // ------------------------------ forwarder (peer CTA): tiles landed
+      bool ok = true;
+      if (has_lora) {
+        ok = mbar_wait(lorabar, 0, ab);
+        if (ok) mbar_arrive_cluster(mapa(lorafwd, 0));
+      }
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int slot = kb % S;
+        const uint32_t par = (kb / S) & 1;
+        if (!mbar_wait(fullA0 + 8 * slot, par, ab) || !mbar_wait(fullB0 + 8 * slot, par, ab)) break;
+        mbar_arrive_cluster(fullB_lead + 8 * slot);
+        *reinterpret_cast<volatile int*>(&consumed) = kb + 1;
+      }
     }
   } else {
     // ------------------------------------------------ dequant warps (2..9)
-    // Thread dt owns, per stage: forward tile row dt (weight row n0 + dt,
-    // block kb); dX the 32 codes [32 hf, 32 hf + 32) of block n0/64 + qb4 of
-    // weight rows 64 kb + 2p and +1 (p = dt % 32, qb4 = dt / 64, hf = dt / 32
-    // % 2: a warp's 32 lanes then write one shared row's 32 distinct words).
-    // Raw codes and scales are loaded two stages ahead.
+    // Forward: TPR threads share a tile row (weight row nh0 + dt / TPR of
+    // block kb), each converting CW 4-byte code words (8 elements, one
+    // 16-byte chunk each).  dX: warp (qb, part) = ((w-2) / 4, (w-2) % 4),
+    // lane p: weight rows 64 kb + 2p and +1, code bytes [8 part, 8 part + 8)
+    // of block nh0 / 64 + qb, i.e. 16 output columns; a warp's 32 lanes
+    // write one shared row's 32 distinct words.  Raw codes and scales are
+    // loaded two stages ahead.
+    constexpr int TPR = 256 / BNH;  // forward: threads a row (2 or 4)
+    constexpr int CW = 8 / TPR;     // forward: code words a thread (4 or 2)
+    constexpr int QB = BNH / 64;    // dX: quant blocks of a weight row a CTA covers (2 or 1)
     const int dt = tid - 64;
     const int fmt = g.w.fmt;
     const int nbk = K / 64;
     const uint8_t* qb = static_cast<const uint8_t*>(g.w.q);
-    const int p = dt & 31, qb4 = dt >> 6, hf = (dt >> 5) & 1;
+    const int frow = dt / TPR, fpart = dt % TPR;
+    const int dq = (warp - 2) >> 2, dpart = (warp - 2) & 3, p = lane;
+    const bool dx_active = dq < QB;
     const uint32_t lut_lane = smem_u32(lutp) + (uint32_t)(lane & (kLutReps - 1)) * 8;
     // (T[lo], T[hi]) of byte J of `w`: one byte permute, one multiply-add, one 8-byte load
     auto lut_at = [&](uint32_t w, int j) -> float2 {
@@ -339,26 +456,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
       return v;
     };
     struct Raw {
-      uint4 c[2];  // forward: 32 code bytes of the row; dX: 16 bytes of each of the two rows
+      uint32_t c[4];  // forward: CW code words of the row; dX: 2 words of each of the two rows
       uint32_t c2b[2];
       float sraw[2];
     };
     auto fetch = [&](int kb, Raw& r) {
-      r.c[0] = r.c[1] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r.c[i] = 0u;
       r.c2b[0] = r.c2b[1] = 0u;
       r.sraw[0] = r.sraw[1] = 0.0f;
       if (kb >= nkb) return;
 #pragma unroll
       for (int h = 0; h < (DX ? 2 : 1); ++h) {
-        const int n = DX ? kb * 64 + 2 * p + h : n0 + dt;
-        const int blk = DX ? (n0 >> 6) + qb4 : kb;
-        if (DX ? blk < nbk : n < N) {
-          const uint4* src = reinterpret_cast<const uint4*>(qb + (size_t)n * (K / 2) + (size_t)blk * 32);
+        const int n = DX ? kb * 64 + 2 * p + h : nh0 + frow;
+        const int blk = DX ? (nh0 >> 6) + dq : kb;
+        if (DX ? (dx_active && blk < nbk) : n < N) {
+          const uint8_t* src = qb + (size_t)n * (K / 2) + (size_t)blk * 32;
           if (DX) {
-            r.c[h] = __ldg(src + hf);
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + dpart);
+            r.c[2 * h] = v.x;
+            r.c[2 * h + 1] = v.y;
+          } else if (CW == 4) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + fpart);
+            r.c[0] = v.x;
+            r.c[1] = v.y;
+            r.c[2] = v.z;
+            r.c[3] = v.w;
           } else {
-            r.c[0] = __ldg(src);
-            r.c[1] = __ldg(src + 1);
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + fpart);
+            r.c[0] = v.x;
+            r.c[1] = v.y;
           }
           const int64_t bi = (int64_t)n * nbk + blk;
           if (fmt == RQ_W_NF4) {
@@ -371,41 +498,44 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
       }
     };
     auto convert = [&](int kb, const Raw& r) -> bool {
-      const int slot = kb % kStages;
+      const int slot = kb % S;
       float sv[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) sv[h] = fmt == RQ_W_NF4 ? r.sraw[h] : sclut[r.c2b[h]] * r.sraw[h];
-      if (kb >= kStages && !mbar_wait(empty0 + 8 * slot, ((kb / kStages) - 1) & 1, abortp)) return false;
-      unsigned char* bt = sm + kSmB + slot * kBBytes;
+      // warp-uniform: every lane of the warp goes on to the same __syncwarp
+      const bool free_slot = kb < S || mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
+      if (!__all_sync(0xffffffffu, free_slot)) return false;
+      unsigned char* bt = sm + TL::kSmB + slot * kBBytes;
       if (DX) {
-        // tile row k (= output column), 16-bit pair (n, n+1) at column 2p
-        const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
-        const uint32_t w0[4] = {r.c[0].x, r.c[0].y, r.c[0].z, r.c[0].w};
-        const uint32_t w1[4] = {r.c[1].x, r.c[1].y, r.c[1].z, r.c[1].w};
+        if (dx_active) {
+          // tile row kr (= output column), 16-bit pair (n, n+1) at word p
+          const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < 2; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 l0 = lut_at(w0[i], j), l1 = lut_at(w1[i], j);
-            const int kr = qb4 * 64 + hf * 32 + i * 8 + j * 2;  // tile rows kr (low nibbles), kr + 1 (high)
-            unsigned char* r0 = bt + (kr >> 3) * 1024 + (kr & 7) * 128 + colo;
-            unsigned char* r1 = bt + ((kr + 1) >> 3) * 1024 + ((kr + 1) & 7) * 128 + colo;
-            *reinterpret_cast<uint32_t*>(r0 + ((colb ^ (kr & 7)) << 4)) = pack_rn<DT>(l0.x * sv[0], l1.x * sv[1]);
-            *reinterpret_cast<uint32_t*>(r1 + ((colb ^ ((kr + 1) & 7)) << 4)) = pack_rn<DT>(l0.y * sv[0], l1.y * sv[1]);
-          }
+            for (int j = 0; j < 4; ++j) {
+              const float2 l0 = lut_at(r.c[i], j), l1 = lut_at(r.c[2 + i], j);
+              const int kr = dq * 64 + dpart * 16 + i * 8 + j * 2;  // tile rows kr (low nibbles), kr + 1 (high)
+              unsigned char* r0 = bt + (kr >> 3) * 1024 + (kr & 7) * 128 + colo;
+              unsigned char* r1 = bt + ((kr + 1) >> 3) * 1024 + ((kr + 1) & 7) * 128 + colo;
+              *reinterpret_cast<uint32_t*>(r0 + ((colb ^ (kr & 7)) << 4)) = pack_rn<DT>(l0.x * sv[0], l1.x * sv[1]);
+              *reinterpret_cast<uint32_t*>(r1 + ((colb ^ ((kr + 1) & 7)) << 4)) =
+                  pack_rn<DT>(l0.y * sv[0], l1.y * sv[1]);
+            }
+        }
       } else {
         // 8 chunks of 16 bytes (8 elements) a row; chunk c at (c ^ (row & 7))
-        const uint32_t cw[8] = {r.c[0].x, r.c[0].y, r.c[0].z, r.c[0].w, r.c[1].x, r.c[1].y, r.c[1].z, r.c[1].w};
-        unsigned char* rowp = bt + (dt >> 3) * 1024 + (dt & 7) * 128;
+        unsigned char* rowp = bt + (frow >> 3) * 1024 + (frow & 7) * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int i = 0; i < CW; ++i) {
+          const int c = fpart * CW + i;
           uint32_t qv[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 l = lut_at(cw[c], j);
+            const float2 l = lut_at(r.c[i], j);
             qv[j] = pack_rn<DT>(l.x * sv[0], l.y * sv[0]);
           }
-          *reinterpret_cast<uint4*>(rowp + ((c ^ (dt & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
+          *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
@@ -425,40 +555,44 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
     }
 
     // ---------------------------------------------------------- epilogue
-    const bool ok = mbar_wait(accbar, 0, abortp) && !*abortp;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int quad = warp & 3;  // tensor-memory lanes 32*quad ... are this warp's rows
-    const int row = quad * 32 + lane, m = m0 + row;
-    const int c_lo = ((warp - 2) >> 2) * (BN / 2);  // warps w and w+4 split the columns
-    const bool has_bias = !DX && g.bias != nullptr;
-    T* y = static_cast<T*>(g.y);
-    for (int cb = c_lo; cb < c_lo + BN / 2; cb += 32) {
-      float acc[32], u[32];
-      tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + cb, acc);
-      if (has_lora) tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + 256 + cb, u);
-      if (!ok || m >= M) continue;
-      uint32_t pk[16];
+    bool ok = mbar_wait(accbar, 0, ab) && !ab.raised();
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int quad = warp & 3;  // tensor-memory lanes 32*quad ... are this warp's rows
+      const int row = quad * 32 + lane, m = m0 + row;
+      const int c_lo = ((warp - 2) >> 2) * (BN / 2);  // warps w and w+4 split the columns
+      const bool has_bias = !DX && g.bias != nullptr;
+      T* y = static_cast<T*>(g.y);
+      for (int cb = c_lo; cb < c_lo + BN / 2; cb += 32) {
+        float acc[32], u[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + cb, acc);
+        if (has_lora) tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + BN + cb, u);
+        if (m >= M) continue;
+        uint32_t pk[16];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        float o[2];
+        for (int j = 0; j < 32; j += 2) {
+          float o[2];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int n = n0 + cb + j + e;
-          const float bv = (has_bias && n < W_out) ? load_scalar(g.bias, g.bdt, n) : 0.0f;
-          o[e] = lora_epilogue<DT>(acc[j + e], has_bias, bv, has_lora ? u[j + e] : 0.0f, has_lora, g.s);
+          for (int e = 0; e < 2; ++e) {
+            const int n = n0 + cb + j + e;
+            const float bv = (has_bias && n < W_out) ? load_scalar(g.bias, g.bdt, n) : 0.0f;
+            o[e] = lora_epilogue<DT>(acc[j + e], has_bias, bv, has_lora ? u[j + e] : 0.0f, has_lora, g.s);
+          }
+          pk[j / 2] = pack_rn<DT>(o[0], o[1]);
         }
-        pk[j / 2] = pack_rn<DT>(o[0], o[1]);
-      }
-      T* yrow = y + (size_t)m * W_out + n0 + cb;
-      if (n0 + cb + 32 <= W_out && ((reinterpret_cast<uintptr_t>(yrow) & 15) == 0)) {
+        T* yrow = y + (size_t)m * W_out + n0 + cb;
+        if (n0 + cb + 32 <= W_out && ((reinterpret_cast<uintptr_t>(yrow) & 15) == 0)) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          reinterpret_cast<uint4*>(yrow)[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-      } else {
-        for (int j = 0; j < 32 && n0 + cb + j < W_out; ++j) {
-          const uint32_t w2 = pk[j / 2];
-          const uint16_t hbits = (j & 1) ? (uint16_t)(w2 >> 16) : (uint16_t)(w2 & 0xFFFF);
-          reinterpret_cast<uint16_t*>(yrow)[j] = hbits;
+          for (int q4 = 0; q4 < 4; ++q4)
+            reinterpret_cast<uint4*>(yrow)[q4] =
+                make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        } else {
+          for (int j = 0; j < 32 && n0 + cb + j < W_out; ++j) {
+            const uint32_t w2 = pk[j / 2];
+            const uint16_t hbits = (j & 1) ? (uint16_t)(w2 >> 16) : (uint16_t)(w2 & 0xFFFF);
+            reinterpret_cast<uint16_t*>(yrow)[j] = hbits;
+          }
         }
       }
     }
@@ -467,26 +601,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ Ge
   // ---------------------------------------------------------- teardown
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 1) {
-    if (*abortp && lane == 0) {
-      // MMAs may still be in flight: wait (bounded) for all of them, and for
-      // the TMA copies the producer issued but no MMA waited for, before
-      // the tensor and shared memory are released
-      mma_commit(drainbar);
-      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(drainbar, 0); ++i) {
-      }
-      const int done = *reinterpret_cast<volatile int*>(&mma_done), issued = *reinterpret_cast<volatile int*>(&a_issued);
-      for (int kb = done; kb < issued; ++kb)
-        for (uint32_t i = 0; i < kWaitLimit && !mbar_test(fullA0 + 8 * (kb % kStages), (kb / kStages) & 1); ++i) {
-        }
-      if (has_lora)
-        for (uint32_t i = 0; i < kWaitLimit && !mbar_test(lorabar, 0); ++i) {
-        }
+  if (warp == 1 && lane == 0 && ab.raised()) {
+    // Work may still be in flight: the leader waits (bounded) for all of its
+    // MMAs; each CTA for the TMA copies its producer issued that nothing
+    // waited for, before the shared and tensor memory are released
+    if (rank == 0) {
+      mma_commit_pair(drainbar, 1);
+      mbar_drain(drainbar, 0);
     }
-    __syncwarp();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    const int done = *reinterpret_cast<volatile int*>(&consumed), issued = *reinterpret_cast<volatile int*>(&a_issued);
+    for (int kb = done; kb < issued; ++kb) mbar_drain(fullA0 + 8 * (kb % S), (kb / S) & 1);
+    if (has_lora) mbar_drain(lorabar, 0);
   }
+  // the peer's shared memory stays alive until the leader's MMAs are done,
+  // and no remote arrive or commit can reach a CTA that has left
+  __syncwarp();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TL::kTmemCols) : "memory");
 }
 
 }  // namespace
@@ -500,7 +634,43 @@ bool gemm_supported(const LinearArgs& a, bool dx) {
   if (a.r > 64 || (a.r > 0 && a.r % 8)) return false;
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
   if (a.r > 0 && (uintptr_t)a.lora_b % 16) return false;
+  if ((dx ? a.w.K : a.w.N) > 65535LL * 128 || a.M > 65535LL * 256) return false;  // grid y and z
   return a.w.N <= 0x7fffffff && a.w.K <= 0x7fffffff && a.M <= 0x7fffffff;
+}
+
+template <int DT, bool DX, int BN>
+static int gemm_run(const GemmArgs& g, uint64_t wout, uint64_t M, cudaStream_t st) {
+  constexpr uint32_t smem = Tile<BN>::kSmBytes;
+  const void* kern = (const void*)gemm_k<DT, DX, BN>;
+  const int rc = ensure_smem_limit(kern, smem);
+  if (rc != RQ_OK) return rc;
+  // CTA pairs along x, output tiles along y, 256-row token pairs along z
+  // (consecutive clusters share X rows); the cluster shape is given at
+  // launch as well
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2u, (unsigned)((wout + BN - 1) / BN), (unsigned)((M + 255) / 256));
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_k<DT, DX, BN>, g);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return RQ_ERR_CUDA;
+  }
+  return check_launch();
+}
+
+// Tile width: 256 outputs a pair unless that leaves SMs idle, then 128.
+static int pick_bn(uint64_t wout, uint64_t M) {
+  const uint64_t ctas256 = 2 * ((wout + 255) / 256) * ((M + 255) / 256);
+  return ctas256 < (uint64_t)num_sms() ? 128 : 256;
 }
 
 // Shared launch of both variants: `a_op` is X (forward) or dY (dX), `t` the
@@ -509,6 +679,7 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
   GemmArgs g;
   const uint64_t M = (uint64_t)a.M, N = (uint64_t)a.w.N, K = (uint64_t)a.w.K, r = (uint64_t)(a.r > 0 ? a.r : 8);
   const uint64_t red = dx ? N : K, wout = dx ? K : N;
+  const int bn = pick_bn(wout, M);
   const int ty = CU_TENSOR_MAP_DATA_TYPE_UINT16;
   const int swz = CU_TENSOR_MAP_SWIZZLE_128B;
   {
@@ -526,9 +697,9 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
       const uint64_t db[3] = {K, r, 1}, sb[2] = {K * 2, 0};
       const uint32_t bb[3] = {64, 64, 1};
       rc = tensor_map_encode(ty, swz, 2, a.lora_a, db, sb, bb, &g.bmap);
-    } else {  // B [N][r]
+    } else {  // B [N][r]: a CTA's bn/2 rows
       const uint64_t db[3] = {r, N, 1}, sb[2] = {r * 2, 0};
-      const uint32_t bb[3] = {BK, BN, 1};
+      const uint32_t bb[3] = {BK, (uint32_t)(bn / 2), 1};
       rc = tensor_map_encode(ty, swz, 2, a.lora_b, db, sb, bb, &g.bmap);
     }
     if (rc != RQ_OK) return rc;
@@ -545,23 +716,13 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
   g.K = (int)K;
   g.r = a.r > 0 ? a.r : 0;
   g.s = dx ? 1.0f : a.scaling;
-  const dim3 grid((unsigned)((wout + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  const void* kern = a.xdt == RQ_BF16 ? (dx ? (const void*)gemm_k<RQ_BF16, true> : (const void*)gemm_k<RQ_BF16, false>)
-                                      : (dx ? (const void*)gemm_k<RQ_F16, true> : (const void*)gemm_k<RQ_F16, false>);
-  const int rc = ensure_smem_limit(kern, kSmBytes);
-  if (rc != RQ_OK) return rc;
   if (a.xdt == RQ_BF16) {
     if (dx)
-      gemm_k<RQ_BF16, true><<<grid, kThreads, kSmBytes, st>>>(g);
-    else
-      gemm_k<RQ_BF16, false><<<grid, kThreads, kSmBytes, st>>>(g);
-  } else {
-    if (dx)
-      gemm_k<RQ_F16, true><<<grid, kThreads, kSmBytes, st>>>(g);
-    else
-      gemm_k<RQ_F16, false><<<grid, kThreads, kSmBytes, st>>>(g);
+      return bn == 256 ? gemm_run<RQ_BF16, true, 256>(g, wout, M, st) : gemm_run<RQ_BF16, true, 128>(g, wout, M, st);
+    return bn == 256 ? gemm_run<RQ_BF16, false, 256>(g, wout, M, st) : gemm_run<RQ_BF16, false, 128>(g, wout, M, st);
   }
-  return check_launch();
+  if (dx) return bn == 256 ? gemm_run<RQ_F16, true, 256>(g, wout, M, st) : gemm_run<RQ_F16, true, 128>(g, wout, M, st);
+  return bn == 256 ? gemm_run<RQ_F16, false, 256>(g, wout, M, st) : gemm_run<RQ_F16, false, 128>(g, wout, M, st);
 }
 
 int gemm_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) { return gemm_launch(a, false, a.x, tdown, st); }

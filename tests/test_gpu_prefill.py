@@ -23,6 +23,7 @@ CASES = [
     (768, 512, 130, 0, False, torch.bfloat16, True),     # no adapter, plain bf16 scales
     (520, 1024, 256, 16, False, torch.float16, True),    # fp16 activations and scales
     (4096, 4096, 512, 64, True, torch.bfloat16, False),  # a configs[2] layer at M=512, r=64
+    (4000, 512, 1200, 16, True, torch.bfloat16, True),   # 256-wide pair tiles (>= 148 CTAs), ragged N and M
 ]
 
 
@@ -58,6 +59,7 @@ DX_CASES = [
     (1024, 2048, 200, 16, True, torch.bfloat16),   # ragged M tile, K not a multiple of 256
     (640, 768, 130, 0, False, torch.float16),
     (4096, 4096, 512, 64, True, torch.bfloat16),
+    (1024, 4032, 1200, 16, True, torch.bfloat16),  # 256-wide pair tiles, K tile past the last quant block
 ]
 
 
