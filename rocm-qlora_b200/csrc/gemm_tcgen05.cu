@@ -28,16 +28,18 @@
 //            operands K-major from shared memory, B of the dX LoRA product
 //            MN-major) and commits each stage to the stage-free barriers of
 //            BOTH CTAs (tcgen05.commit multicast); in the peer CTA lane 0
-//            forwards "both of this CTA's tiles of the stage are ready" to the
-//            leader, the one cluster-scope release a stage (a thread with no
-//            loads in flight, so the release costs no wait);
+//            signals "both of this CTA's tiles of the stage are ready" to the
+//            leader with a 16-byte bulk copy into the leader's shared memory
+//            whose completion lands on the leader's fullB (no fence in the
+//            signalling thread, so the signals pipeline);
 //   warps 2-9  dequantize this CTA's half of the weight tile of each stage
 //            as the reference's exact bf16/f16(T[code] * scale) values into
 //            the swizzled K-major layout, arrive on their CTA's fullB, then
 //            run the epilogue on this CTA's 128 rows: tcgen05.ld of both
 //            accumulators, bias and LoRA rounding, Y stores.
-// Barriers: fullA (own TMA bytes), fullB (own 8 dequant warps, plus the
-// peer's forward in the leader), empty (MMA commit), lora / lorafwd, acc
+// Barriers: fullA (own TMA bytes), fullB (own 8 dequant warps; in the
+// leader also its producer's expect_tx for the peer's signal), empty (MMA
+// commit), lora / lorafwd (the peer's LoRA-tile signal), acc
 // (final commit, both CTAs).  Grid (2, output tiles, token pairs): the
 // clusters that run together share token rows, so X stays in L2.  Every wait is
 // bounded; a wait that runs out raises the abort flag of both CTAs, each
@@ -81,7 +83,9 @@ constexpr int BK = 64;
 constexpr int kDqWarps = 8;                 // dequant / epilogue warps
 constexpr int kThreads = 64 + kDqWarps * 32;
 constexpr uint32_t kABytes = BM * BK * 2;   // 16 KB
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr uint32_t kWaitLimit = 1u << 22;   // polls of a bounded wait (each at least kPollNs apart)
+constexpr uint32_t kPollNs = 32;
+constexpr int kPrefetch = 4;                // stages of codes and scales a dequant thread holds in registers
 constexpr int kLutReps = 16;                // copies of the code-byte table (one per half-warp lane)
 constexpr uint32_t kLutBytes = 256 * kLutReps * 8;
 constexpr uint32_t kSmemCap = 226 * 1024;   // dynamic shared memory budget (static + margin in the last KB)
@@ -148,23 +152,32 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// arrive (release at cluster scope) on a barrier given by its shared::cluster address
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+// Signal a barrier of the peer CTA without a fence in this thread: a 16-byte
+// shared-to-peer-shared bulk copy whose completion adds 16 transaction bytes
+// to the peer's barrier `cbar` (dst and cbar are shared::cluster addresses).
+// The receiving CTA posts the matching expect_tx.  A release-arrive at
+// cluster scope would wait for this thread's previous remote operations to
+// be acknowledged (about a microsecond a stage).
+__device__ __forceinline__ void bulk_signal(uint32_t cdst, uint32_t src, uint32_t cbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], 16, [%2];" ::"r"(cdst),
+               "r"(src), "r"(cbar)
+               : "memory");
 }
+// Non-blocking test of a phase (test_wait: the thread is never suspended,
+// so it sees the completion as soon as it happens).
 template <bool kCluster>
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   if constexpr (kCluster)
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(bar), "r"(parity)
         : "memory");
   else
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(bar), "r"(parity)
         : "memory");
@@ -189,14 +202,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const A
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_test<kCluster>(bar, parity)) return true;
     if (ab.raised()) return false;
+    __nanosleep(kPollNs);  // a paced poll: the barrier word is not hammered
   }
   ab.raise();
   atomicAdd(&g_gemm_timeouts, 1u);
   return false;
 }
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit && !mbar_test<false>(bar, parity); ++i) {
-  }
+  for (uint32_t i = 0; i < kWaitLimit && !mbar_test<false>(bar, parity); ++i) __nanosleep(kPollNs);
 }
 
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -273,6 +286,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Read-only global loads pinned where they are written (volatile asm): the
+// dequant warps' prefetch of codes and scales must be issued stages ahead
+// of its use, not sunk to it by the compiler.
+__device__ __forceinline__ uint4 ldg_pin4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint2 ldg_pin2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_pin_u8(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u8 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float ldg_pin_f32(const void* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // two fp32 values rounded to the 16-bit type DT (one packed convert)
 template <int DT>
 __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
@@ -296,6 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
   __shared__ __align__(8) uint64_t bars[3 * S + 4];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag, a_issued, consumed;
+  __shared__ __align__(16) uint32_t sig_src[4], sig_dst[4];  // the 16-byte signal copies (contents unused)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();  // 0: leader (issues the pair's MMAs), 1: peer
   // 1 KB aligned view of the dynamic shared memory (swizzle atoms); the
@@ -318,7 +359,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(fullA0 + 8 * i, 1);
-      mbar_init(fullB0 + 8 * i, rank == 0 ? kDqWarps + 1 : kDqWarps);
+      mbar_init(fullB0 + 8 * i, rank == 0 ? kDqWarps + 1 : kDqWarps);  // leader: + its producer's expect_tx
       mbar_init(empty0 + 8 * i, 1);
     }
     mbar_init(lorabar, 1);
@@ -328,6 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
     abort_flag = 0;
     a_issued = 0;
     consumed = 0;
+    for (int i = 0; i < 4; ++i) sig_src[i] = sig_dst[i] = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // whole warp, in both CTAs: the pair's tensor memory
@@ -357,11 +399,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base_sh;
   const uint32_t fullB_lead = mapa(fullB0, 0);  // the leader's fullB[0] (cluster address)
+  const uint32_t sig_lead = mapa(smem_u32(sig_dst), 0);
 
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
     if (lane == 0) {
       if (has_lora) {
+        if (rank == 0) mbar_expect_tx(lorafwd, 16);  // the peer's "LoRA tiles landed" signal
         mbar_expect_tx(lorabar, kABytes + kBBytes);
         tma_2d(sbase + TL::kSmT, &g.tmap, 0, m0, lorabar);
         if (DX) {
@@ -374,6 +418,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       for (int kb = 0; kb < nkb; ++kb) {
         const int slot = kb % S;
         if (kb >= S && !mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab)) break;
+        if (rank == 0) mbar_expect_tx(fullB0 + 8 * slot, 16);  // the peer's "stage ready" signal
         mbar_expect_tx(fullA0 + 8 * slot, kABytes);
         tma_2d(sbase + TL::kSmA + slot * kABytes, &g.xmap, kb * BK, m0, fullA0 + 8 * slot);
         *reinterpret_cast<volatile int*>(&a_issued) = kb + 1;
@@ -418,13 +463,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       bool ok = true;
       if (has_lora) {
         ok = mbar_wait(lorabar, 0, ab);
-        if (ok) mbar_arrive_cluster(mapa(lorafwd, 0));
+        if (ok) bulk_signal(mapa(smem_u32(sig_dst), 0), smem_u32(sig_src), mapa(lorafwd, 0));
       }
       for (int kb = 0; kb < nkb && ok; ++kb) {
         const int slot = kb % S;
         const uint32_t par = (kb / S) & 1;
         if (!mbar_wait(fullA0 + 8 * slot, par, ab) || !mbar_wait(fullB0 + 8 * slot, par, ab)) break;
-        mbar_arrive_cluster(fullB_lead + 8 * slot);
+        bulk_signal(sig_lead, smem_u32(sig_src), fullB_lead + 8 * slot);
         *reinterpret_cast<volatile int*>(&consumed) = kb + 1;
       }
     }
@@ -436,7 +481,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
     // lane p: weight rows 64 kb + 2p and +1, code bytes [8 part, 8 part + 8)
     // of block nh0 / 64 + qb, i.e. 16 output columns; a warp's 32 lanes
     // write one shared row's 32 distinct words.  Raw codes and scales are
-    // loaded two stages ahead.
+    // loaded kPrefetch stages ahead.
     constexpr int TPR = 256 / BNH;  // forward: threads a row (2 or 4)
     constexpr int CW = 8 / TPR;     // forward: code words a thread (4 or 2)
     constexpr int QB = BNH / 64;    // dX: quant blocks of a weight row a CTA covers (2 or 1)
@@ -473,17 +518,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         if (DX ? (dx_active && blk < nbk) : n < N) {
           const uint8_t* src = qb + (size_t)n * (K / 2) + (size_t)blk * 32;
           if (DX) {
-            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + dpart);
+            const uint2 v = ldg_pin2(reinterpret_cast<const uint2*>(src) + dpart);
             r.c[2 * h] = v.x;
             r.c[2 * h + 1] = v.y;
           } else if (CW == 4) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + fpart);
+            const uint4 v = ldg_pin4(reinterpret_cast<const uint4*>(src) + fpart);
             r.c[0] = v.x;
             r.c[1] = v.y;
             r.c[2] = v.z;
             r.c[3] = v.w;
           } else {
-            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + fpart);
+            const uint2 v = ldg_pin2(reinterpret_cast<const uint2*>(src) + fpart);
             r.c[0] = v.x;
             r.c[1] = v.y;
           }
@@ -491,8 +536,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
           if (fmt == RQ_W_NF4) {
             r.sraw[h] = load_scalar(g.w.scales, g.w.sdt, bi);
           } else {
-            r.c2b[h] = __ldg(g.w.c2 + bi);
-            r.sraw[h] = __ldg(g.w.c2s + bi / kDQBlock2);
+            r.c2b[h] = ldg_pin_u8(g.w.c2 + bi);
+            r.sraw[h] = ldg_pin_f32(g.w.c2s + bi / kDQBlock2);
           }
         }
       }
@@ -502,9 +547,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       float sv[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) sv[h] = fmt == RQ_W_NF4 ? r.sraw[h] : sclut[r.c2b[h]] * r.sraw[h];
-      // warp-uniform: every lane of the warp goes on to the same __syncwarp
-      const bool free_slot = kb < S || mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
-      if (!__all_sync(0xffffffffu, free_slot)) return false;
+      // lane 0 polls the barrier (the other lanes wait in the shuffle, so
+      // the shared-memory pipe the TMA writes through is not flooded with
+      // polls), and the warp takes one decision
+      bool free_slot = true;
+      if (kb >= S && lane == 0) free_slot = mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
+      if (!__shfl_sync(0xffffffffu, (int)free_slot, 0)) return false;
       unsigned char* bt = sm + TL::kSmB + slot * kBBytes;
       if (DX) {
         if (dx_active) {
@@ -543,20 +591,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       if (lane == 0) mbar_arrive(fullB0 + 8 * slot);
       return true;
     };
-    Raw ra, rb;
-    fetch(0, ra);
-    fetch(1, rb);
-    for (int kb = 0; kb < nkb; kb += 2) {
-      if (!convert(kb, ra)) break;
-      fetch(kb + 2, ra);
-      if (kb + 1 >= nkb) break;
-      if (!convert(kb + 1, rb)) break;
-      fetch(kb + 3, rb);
+    // a register ring of kPrefetch stages (static indices: fully unrolled)
+    Raw ring[kPrefetch];
+#pragma unroll
+    for (int i = 0; i < kPrefetch; ++i) fetch(i, ring[i]);
+    bool go = true;
+    for (int kb = 0; kb < nkb && go; kb += kPrefetch) {
+#pragma unroll
+      for (int i = 0; i < kPrefetch; ++i) {
+        if (go && kb + i < nkb) {
+          go = convert(kb + i, ring[i]);
+          fetch(kb + i + kPrefetch, ring[i]);
+        }
+      }
     }
 
     // ---------------------------------------------------------- epilogue
-    bool ok = mbar_wait(accbar, 0, ab) && !ab.raised();
-    ok = __all_sync(0xffffffffu, ok);
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait(accbar, 0, ab) && !ab.raised();
+    ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
     if (ok) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int quad = warp & 3;  // tensor-memory lanes 32*quad ... are this warp's rows
@@ -614,9 +667,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
     if (has_lora) mbar_drain(lorabar, 0);
   }
   // the peer's shared memory stays alive until the leader's MMAs are done,
-  // and no remote arrive or commit can reach a CTA that has left
+  // and no remote arrive, signal or commit can reach a CTA that has left.
+  // On the normal path the leader consumed every signal the peer sent; after
+  // an abort the peer's last signals may still be in flight: the leader
+  // gives them a bounded time to land between two cluster barriers (both
+  // CTAs pass both barriers on every path).
   __syncwarp();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync();
+  if (tid == 0 && rank == 0 && ab.raised()) {
+    uint64_t t0, t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+      __nanosleep(1000);
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    } while (t1 - t0 < 50000);  // 50 us
+  }
   cluster_sync();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (warp == 1)
