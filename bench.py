@@ -24,7 +24,10 @@ before the timed region as well as during it, so short timed regions still
 get samples under load.
 With N > 1 (torchrun), each rank holds a column shard: the sweep's layers
 have N times the output features, every rank runs its [N_shape, K] shard,
-and Y is all-gathered over NCCL (weak scaling).
+and Y is gathered on every rank (weak scaling): by default inside the GEMV
+(each rank's epilogue stores its columns into every rank's full output over
+NVLink and the ranks meet at the end of the kernel), with --gather nccl by
+an NCCL all-gather after the layer.
 """
 from __future__ import annotations
 
@@ -168,11 +171,16 @@ def run_ours(args, rank, world, device):
     B = [lo.lora_B.detach().to(torch.bfloat16).contiguous() for lo in layers]
     calls = [(si, M) for si in range(len(SHAPES)) for M in MS]
 
-    gather_out = {}
+    gather_out, peers = {}, {}
+    fused = world > 1 and args.gather == "fused"
     if world > 1:
+        from rocm_qlora.distributed.peer_gather import PeerGather
         for si, (N, K) in enumerate(SHAPES):
             for M in MS:
-                gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
+                if fused:  # this rank's N columns of the full [M, world*N] output, on every rank
+                    peers[(si, M)] = PeerGather(None, M, world * N, rank * N, torch.bfloat16, device)
+                else:
+                    gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
 
     def step(c, lora=True):
         """One sweep pass.  lora=True is the measured step (adapter, and the
@@ -180,7 +188,10 @@ def run_ours(args, rank, world, device):
         dequant GEMV kernels alone, no adapter and no collective."""
         for si, M in calls:
             w = wsets[c][si]
-            if lora:
+            if lora and fused:  # the GEMV writes Y into every rank's output (NVLink), no collective
+                rc = layer_ops.forward_gather(w, xs[(si, M)], None, A[si], B[si], ALPHA / R, peers[(si, M)].descriptor)
+                assert rc == 0, "the fused gather refused a decode call"
+            elif lora:
                 y = layer_ops.forward(w, xs[(si, M)], None, A[si], B[si], ALPHA / R)
                 if world > 1:
                     dist.all_gather_into_tensor(gather_out[(si, M)], y)
@@ -273,6 +284,9 @@ def run_ours(args, rank, world, device):
     # graphs that hold NCCL calls are released before the process group goes
     del graphs, gemv_graphs
     torch.cuda.synchronize(device)
+    gather_error = any(pg.error() for pg in peers.values())
+    for pg in peers.values():
+        pg.close()
 
     # end to end through the public API with host buffers
     e2e = run_e2e(args, rotated_modules(layers, wsets), device, world)
@@ -291,6 +305,9 @@ def run_ours(args, rank, world, device):
                                    "NF4 + double-quant, M in {1,4,16}, LoRA r16 a32",
                        "model": "Llama-2-7B-shaped projections", "global_batch": MS, "seq_len": 1,
                        "parallelism": f"column-shard x{world}" if world > 1 else "single GPU",
+                       "gather": (("fused GEMV epilogue peer stores over NVLink" if fused else "NCCL all-gather")
+                                  if world > 1 else None),
+                       "gather_error": gather_error if world > 1 else None,
                        "l2": f"{copies} rotating weight copies ({copies * per_set / 2**20:.0f} MiB) > 126 MB L2",
                        "graphs": use_graphs},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -575,6 +592,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill GEMM leg")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: gather Y in the GEMV epilogue over NVLink (fused) or with NCCL all-gather")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

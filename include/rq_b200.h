@@ -45,6 +45,7 @@ extern "C" {
 #define RQ_ERR_WORKSPACE (-5)   /* workspace missing or too small */
 #define RQ_ERR_DEVICE (-6)      /* current device is not sm_100 */
 #define RQ_ERR_SCRATCH (-7)     /* needs more than rq_linear_forward_noalloc's built-in scratch */
+#define RQ_ERR_UNSUPPORTED (-8) /* no fused form for these arguments: nothing was launched */
 
 #define RQ_F32 0
 #define RQ_BF16 1
@@ -189,6 +190,65 @@ RQ_API int rq_linear_forward_noalloc(int wfmt, const void* qweight, const void* 
 #define RQ_PATH_GEMV_SLABS 3
 #define RQ_PATH_SIMT 4
 RQ_API int rq_last_path(void);
+
+/* ------------------------------- column shards: fused output gather */
+
+/* Device memory shared with the other ranks of one node (one process per
+ * GPU, NVLink peers).  rq_peer_alloc returns a zero-filled cudaMalloc
+ * allocation of `bytes` on the current device; rq_peer_handle writes its
+ * 64-byte IPC handle to `handle` (the caller ships it to the other ranks);
+ * rq_peer_open maps another rank's allocation into this process for the
+ * current device (peer access enabled) and rq_peer_close unmaps it.
+ * Plumbing for rq_linear_forward_gather; no counterpart in the reference,
+ * which replicates layers instead of sharding them. */
+RQ_API int rq_peer_alloc(int64_t bytes, void** ptr);
+RQ_API int rq_peer_free(void* ptr);
+RQ_API int rq_peer_handle(const void* ptr, void* handle);
+RQ_API int rq_peer_open(const void* handle, void** ptr);
+RQ_API int rq_peer_close(void* ptr);
+
+/* The node-wide output of a column-sharded layer: every rank computes the
+ * output features [col, col + N) of the full Y[M, ld] and writes them into
+ * EVERY rank's copy of Y.  All pointers are device pointers valid on this
+ * rank (peer allocations opened with rq_peer_open):
+ *   outs[q]      rank q's Y (row stride ld elements of xdtype), q < world
+ *   flags[q]     rank q's flag array, `world` uint32 (zero before first use)
+ *   my_flags     this rank's flag array (== flags[rank])
+ *   ctrl         this rank's 4 uint32 of control state, zero before first
+ *                use: [0] arrival counter (kernels leave it zero), [1] epoch
+ *                (calls so far), [2] error (set to 1 if a peer did not
+ *                arrive within about 2 s; the output is then incomplete)
+ * outs and flags are device arrays of `world` pointers. */
+typedef struct RqGather {
+  void* const* outs;
+  uint32_t* const* flags;
+  uint32_t* my_flags;
+  uint32_t* ctrl;
+  int64_t ld;
+  int64_t col;
+  int world;
+  int rank;
+} RqGather;
+
+/* rq_linear_forward of this rank's shard (W is [N, K], the shard's rows)
+ * whose output is written into every rank's Y[:, col:col+N] instead of a
+ * local y; when the kernel has completed on a rank, every rank's shard of
+ * this call is in that rank's Y (the ranks meet at the end of the kernel:
+ * the last CTA publishes this call's epoch to every rank's flags and waits,
+ * bounded, for all of theirs).  Every rank must make the same sequence of
+ * calls with the same M.  A rank's Y is rewritten by the next call that
+ * names it, so the caller consumes each result before issuing a later call
+ * on the same outputs.  Only the fused decode GEMV (NF4 formats, bf16/f16,
+ * M <= 16) has this form: other arguments return RQ_ERR_UNSUPPORTED before
+ * anything is launched, and the caller gathers with a collective instead.
+ * Same-node NVLink peers only; one call in flight per RqGather. */
+RQ_API int rq_linear_forward_gather(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                      const uint8_t* c2, const float* c2_scales,
+                      int64_t N, int64_t K, int block_size,
+                      const void* x, int xdtype, int64_t M,
+                      const void* bias, int bias_dtype,
+                      const void* lora_a, const void* lora_b, int r, float scaling,
+                      const RqGather* gather, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------- reference launcher drop-ins */
 

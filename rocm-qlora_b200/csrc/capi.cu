@@ -100,6 +100,7 @@ static int fill_args(LinearArgs* a, int wfmt, const void* q, const void* scales,
   a->ws = ws;
   a->ws_bytes = ws_bytes;
   a->lora_x = x;
+  a->gather = nullptr;
   return RQ_OK;
 }
 
@@ -229,6 +230,24 @@ int rq_linear_forward(int wfmt, const void* qweight, const void* scales, int sca
   if (rc != RQ_OK) return rc;
   if (lora_x && (uintptr_t)lora_x % dtype_size(xdtype)) return RQ_ERR_ALIGN;
   a.lora_x = lora_x ? lora_x : x;
+  return linear_forward(a, (cudaStream_t)stream);
+}
+
+int rq_linear_forward_gather(int wfmt, const void* qweight, const void* scales, int scale_dtype, const uint8_t* c2,
+                             const float* c2_scales, int64_t N, int64_t K, int block_size, const void* x, int xdtype,
+                             int64_t M, const void* bias, int bias_dtype, const void* lora_a, const void* lora_b, int r,
+                             float scaling, const RqGather* gather, void* workspace, int64_t workspace_bytes,
+                             void* stream) {
+  RQ_PROLOGUE();
+  if (!gather) return RQ_ERR_INVALID;
+  LinearArgs a;
+  // the output is the ranks' Y, not a local y: x stands in for the argument
+  // check (it is never written)
+  int rc = fill_args(&a, wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size, x, xdtype, M, bias,
+                     bias_dtype, lora_a, lora_b, r, scaling, const_cast<void*>(x), workspace, workspace_bytes);
+  if (rc != RQ_OK) return rc;
+  a.y = nullptr;
+  a.gather = gather;
   return linear_forward(a, (cudaStream_t)stream);
 }
 

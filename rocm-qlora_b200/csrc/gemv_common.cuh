@@ -49,6 +49,8 @@ struct GemvArgs {
   int tiles;           // ceil(N / 8)
   int chunks;          // row chunks per CTA
   int xdt;             // activation dtype (RQ_BF16 / RQ_F16)
+  int gather;          // nonzero: output into every rank's Y per gth (NF4 kernel only)
+  RqGather gth;
 };
 
 // mma.sync m16n8k16 with a zero accumulator input (starts a block partial)

@@ -335,7 +335,10 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
   g.s = a.scaling;
   g.y = a.y;
   g.xdt = a.xdt;
+  g.gather = a.gather != nullptr;
+  if (a.gather) g.gth = *a.gather;
   if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_forward(g, a.r > 0, st);
+  if (a.gather) return RQ_ERR_UNSUPPORTED;  // the INT8 kernel has no gather epilogue
   const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;
   int nt = 1;
   gemv_shape(wk, a.w.N, a.w.K, a.M, a.r, &g.grid, &g.tiles, &g.chunks, &nt);

@@ -70,6 +70,48 @@ constexpr int kLoraDownCtas = 8;                  // CTAs of the small-M down-pr
 // Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// The end of a gathering call, run by one thread of every CTA after the
+// CTA's stores are fenced at system scope.  The last CTA of this rank to
+// arrive (all of the rank's stores are then issued and fenced) advances the
+// epoch, publishes it in every rank's flag slot for this rank (release at
+// system scope) and waits, at most about 2 s, until every rank's flag here
+// holds the epoch: from then on every rank's shard of this call is in this
+// rank's Y.  The arrival counter goes back to zero for the next call.
+__device__ void gather_arrive(const RqGather& g) {
+  uint32_t* ctrl = g.ctrl;
+  uint32_t arrived;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(ctrl) : "memory");
+  if (arrived != gridDim.x - 1) return;
+  ctrl[0] = 0;
+  const uint32_t epoch = ctrl[1] + 1;
+  ctrl[1] = epoch;
+  __threadfence_system();
+  for (int q = 0; q < g.world; ++q) {
+    uint32_t* f = g.flags[q] + g.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+  }
+  const uint64_t t0 = global_ns();
+  for (int q = 0; q < g.world; ++q) {
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.my_flags + q) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (global_ns() - t0 > 2000000000ull) {
+        ctrl[2] = 1;
+        atomicAdd(&g_kernel_timeouts, 1u);
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
 struct Nf4Args {
   CUtensorMap wmap;  // codes: 3-D uint8 [N][K/256][128], box 128 x 2 x NT*16 (wide),
                      // else 2-D uint8 [N][K/2], box 128 x NT*16; 128-byte swizzle
@@ -470,7 +512,13 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         for (int j = 0; j < p.r; ++j) uu = fmaf(DType<DT>::to_f32(trow[j]), DType<DT>::to_f32(__ldg(brow + j)), uu);
       }
       const float bv = has_bias ? load_scalar(p.bias, p.bdt, row) : 0.0f;
-      y[(size_t)m * N + row] = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, uu, has_lora, p.s));
+      const T v = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, uu, has_lora, p.s));
+      if (p.gather) {  // into every rank's Y[:, col + row] (NVLink stores to the peers)
+        const size_t o = (size_t)m * p.gth.ld + p.gth.col + row;
+        for (int rq = 0; rq < p.gth.world; ++rq) static_cast<T*>(p.gth.outs[rq])[o] = v;
+      } else {
+        y[(size_t)m * N + row] = v;
+      }
     }
     consumer_sync();  // partial sums (and per-pass scales) are reused by the next pass
   }
@@ -487,6 +535,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     for (uint32_t v = passes; v < nr; ++v)
       for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, v & 1); ++i) {
       }
+  }
+  if (p.gather) {
+    __threadfence_system();  // this thread's stores to the ranks' Y, before the CTA's arrival
+    consumer_sync();
+    if (tid == 0) gather_arrive(p.gth);
   }
 }
 

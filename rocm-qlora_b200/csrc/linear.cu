@@ -75,9 +75,20 @@ static int gemv_slabs(const LinearArgs& a, const void* t, cudaStream_t st) {
   return RQ_OK;
 }
 
+// The fused gather exists for the NF4 decode GEMV only; decided before any
+// launch so that a caller can fall back to a collective.
+static bool gather_eligible(const LinearArgs& a) {
+  if (!is_nf4_fmt(a.w.fmt) || a.M < 1 || a.M > 16 || !gemv_supported(a)) return false;
+  const RqGather& g = *a.gather;
+  if (g.world < 1 || g.world > 64 || g.rank < 0 || g.rank >= g.world || !g.outs || !g.flags || !g.my_flags || !g.ctrl)
+    return false;
+  return g.col >= 0 && g.ld >= g.col + a.w.N;
+}
+
 int linear_forward(const LinearArgs& a, cudaStream_t st) {
   WsView v;
   t_last_path = RQ_PATH_NONE;
+  if (a.gather && !gather_eligible(a)) return RQ_ERR_UNSUPPORTED;
   int rc = carve(a, &v);
   if (rc != RQ_OK) return rc;
   if (a.M == 0 || a.w.N == 0) return RQ_OK;

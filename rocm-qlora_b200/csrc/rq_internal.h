@@ -72,6 +72,7 @@ struct LinearArgs {
   void* y;              // [M, N] (forward) or dx [M, K]
   void* ws;
   int64_t ws_bytes;
+  const RqGather* gather;  // forward only: write the output into every rank's Y (nullptr: local y)
 };
 
 // kernel families (linear.cu picks one per call)

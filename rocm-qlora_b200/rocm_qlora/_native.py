@@ -23,10 +23,18 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("RQ_B200_LIB", os.path.join(_HERE, "librqb200.so"))
 
 RQ_OK = 0
+RQ_ERR_UNSUPPORTED = -8
 F32, BF16, F16 = 0, 1, 2
 W_NF4, W_NF4_DQ_FP8, W_NF4_DQ_INT8, W_INT8, W_INT8_ROW = 0, 1, 2, 3, 4
 
 _DT_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+
+class RqGather(ctypes.Structure):
+    """struct RqGather of include/rq_b200.h (device pointers)."""
+    _fields_ = [("outs", ctypes.c_void_p), ("flags", ctypes.c_void_p), ("my_flags", ctypes.c_void_p),
+                ("ctrl", ctypes.c_void_p), ("ld", ctypes.c_int64), ("col", ctypes.c_int64),
+                ("world", ctypes.c_int), ("rank", ctypes.c_int)]
 
 
 class NativeUnavailable(RuntimeError):
@@ -61,6 +69,13 @@ def _bind(L: ctypes.CDLL) -> None:
         "rq_linear_forward": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, P, I, P, P, I, F, P, P, I64, P], I),
         "rq_linear_dx": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, P, I, F, P, P, I64, P], I),
         "rq_linear_forward_noalloc": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, P, I, P, P, I, F, P, P], I),
+        "rq_linear_forward_gather": ([I, P, P, I, P, P, I64, I64, I, P, I, I64, P, I, P, P, I, F,
+                                      ctypes.POINTER(RqGather), P, I64, P], I),
+        "rq_peer_alloc": ([I64, ctypes.POINTER(ctypes.c_void_p)], I),
+        "rq_peer_free": ([P], I),
+        "rq_peer_handle": ([P, P], I),
+        "rq_peer_open": ([P, ctypes.POINTER(ctypes.c_void_p)], I),
+        "rq_peer_close": ([P], I),
         "launch_int4_dequant_matmul": ([P, P, P, P, P, I, I, I, I], None),
         "launch_int8_dequant_matmul": ([P, P, P, P, P, I, I, I, I], None),
     }
@@ -77,6 +92,8 @@ def exported_symbols() -> Tuple[str, ...]:
             "rq_nf4_quantize", "rq_nf4_dequantize", "rq_int8_quantize", "rq_int8_quantize_rows",
             "rq_int8_dequantize", "rq_dq_quantize_scales", "rq_dq_dequantize",
             "rq_linear_workspace_bytes", "rq_linear_forward", "rq_linear_dx", "rq_linear_forward_noalloc",
+            "rq_linear_forward_gather", "rq_peer_alloc", "rq_peer_free", "rq_peer_handle", "rq_peer_open",
+            "rq_peer_close",
             "launch_int4_dequant_matmul", "launch_int8_dequant_matmul")
 
 

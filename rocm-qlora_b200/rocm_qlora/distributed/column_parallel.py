@@ -11,7 +11,10 @@ of the bias and of LoRA B; LoRA A [r, K] is replicated.
              dB_i, dbias_i stay local
 
 The collectives are NCCL over NVLink (torch.distributed); the per-rank
-layer is the fused B200 QuantLinear / LoRALinear of this package.
+layer is the fused B200 QuantLinear / LoRALinear of this package.  With
+``gather_tokens > 0`` the decode forward (M <= 16, no autograd) skips the
+all-gather: the GEMV writes its shard into every rank's output over NVLink
+and the ranks meet at the end of the kernel (``peer_gather.PeerGather``).
 """
 from typing import List, Optional, Tuple
 
@@ -19,7 +22,10 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from rocm_qlora import _native as nat
+from rocm_qlora.distributed.peer_gather import PeerGather, gather_eligible
 from rocm_qlora.lora.lora_layer import LoRALinear
+from rocm_qlora.quantization import layer_ops
 from rocm_qlora.quantization.quant_linear import QuantLinear
 
 
@@ -92,7 +98,8 @@ class ColumnParallelLinear(nn.Module):
     gradient is all-reduced during backward.
     """
 
-    def __init__(self, local: nn.Module, out_features: int, group=None, granule: int = 16):
+    def __init__(self, local: nn.Module, out_features: int, group=None, granule: int = 16, gather_tokens: int = 0,
+                 gather_dtype: torch.dtype = torch.bfloat16):
         super().__init__()
         self.local = local
         self.group = group
@@ -100,6 +107,10 @@ class ColumnParallelLinear(nn.Module):
         self.world, self.rank = _world(group)
         self.sizes = [b - a for a, b in (shard_range(out_features, self.world, i, granule) for i in range(self.world))]
         self.lo, self.hi = shard_range(out_features, self.world, self.rank, granule)
+        self.peer: Optional[PeerGather] = None
+        if gather_tokens > 0 and self.world > 1 and dist.get_backend(group) == "nccl":
+            dev = next(local.buffers()).device
+            self.peer = PeerGather(group, gather_tokens, out_features, self.lo, gather_dtype, dev)
         lora_a = getattr(local, "lora_A", None)
         if self.world > 1 and isinstance(lora_a, torch.Tensor) and lora_a.requires_grad:
             lora_a.register_hook(self._sum_over_ranks)
@@ -109,9 +120,39 @@ class ColumnParallelLinear(nn.Module):
         dist.all_reduce(g, group=self.group)
         return g
 
+    def _forward_fused(self, x: torch.Tensor) -> Optional[torch.Tensor]:
+        """The gathered output through the fused kernel, or None when this
+        call has no fused form (decided identically on every rank)."""
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if self.peer is None or x2.dtype != self.peer.dtype or not gather_eligible(x2, self.local, self.peer.max_tokens):
+            return None
+        x2 = x2.contiguous()
+        if isinstance(self.local, LoRALinear):
+            base, dt = self.local.base_layer, x2.dtype
+            A, B, s = self.local.lora_A.to(dt).contiguous(), self.local.lora_B.to(dt).contiguous(), self.local.scaling
+        else:
+            base, A, B, s = self.local, None, None, 1.0
+        bias = base.bias.to(x2.dtype).contiguous() if base.bias is not None else None
+        rc = layer_ops.forward_gather(base.weight_view(), x2, bias, A, B, s, self.peer.descriptor)
+        if rc != nat.RQ_OK:
+            # nothing was launched on this rank, but the others may have: a
+            # hang must not follow, so this is an error, not a fallback
+            raise RuntimeError("rq_linear_forward_gather refused a call the ranks agreed to fuse")
+        return self.peer.output(x2.shape[0]).view(*lead, self.out_features)
+
+    def close(self) -> None:
+        """Collective: release the fused-gather buffers (every rank calls it)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return self.local(x)
+        y = self._forward_fused(x)
+        if y is not None:
+            return y
         if torch.is_grad_enabled() and x.requires_grad:
             x = _ReduceGradient.apply(x, self.group)
         y = self.local(x)
@@ -120,7 +161,7 @@ class ColumnParallelLinear(nn.Module):
     @classmethod
     def from_linear(cls, linear: nn.Linear, bits: int = 4, double_quant: bool = True, lora_r: int = 0,
                     lora_alpha: int = 16, lora_dropout: float = 0.0, group=None,
-                    granule: int = 16) -> "ColumnParallelLinear":
+                    granule: int = 16, gather_tokens: int = 0) -> "ColumnParallelLinear":
         """Quantizes this rank's rows of `linear` (every rank passes the same
         full layer) and wraps them, with LoRA adapters when lora_r > 0 (A
         broadcast from rank 0 so all ranks hold the same replica; B starts at
@@ -143,4 +184,6 @@ class ColumnParallelLinear(nn.Module):
                 with torch.no_grad():
                     dist.broadcast(local.lora_A.data, src=dist.get_global_rank(group, 0) if group else 0,
                                    group=group)
-        return cls(local, linear.out_features, group=group, granule=granule)
+        return cls(local, linear.out_features, group=group, granule=granule, gather_tokens=gather_tokens,
+                   gather_dtype=linear.weight.dtype if linear.weight.dtype in (torch.bfloat16, torch.float16)
+                   else torch.bfloat16)

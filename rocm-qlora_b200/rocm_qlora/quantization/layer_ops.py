@@ -6,6 +6,7 @@ current CUDA stream.  The adapter gradients dA / dB are plain cuBLAS matmuls
 in the activation dtype with the same roundings as the reference's autograd
 of ``x @ A.T @ B.T * scaling`` (rocm_qlora/lora/lora_layer.py:67).
 """
+import ctypes
 from dataclasses import dataclass
 from typing import Optional
 
@@ -87,6 +88,30 @@ def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: O
                                       r, float(scaling), y.data_ptr(), ws.data_ptr(), ws.numel(),
                                       nat.stream_ptr(dev)), "rq_linear_forward")
     return y
+
+
+def forward_gather(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: Optional[torch.Tensor],
+                   B: Optional[torch.Tensor], scaling: float, gather) -> int:
+    """This rank's shard of a column-sharded layer written into every rank's
+    output (``gather``: an ``_native.RqGather``).  Returns the library status:
+    RQ_OK, or RQ_ERR_UNSUPPORTED when these arguments have no fused form
+    (nothing was launched; the caller gathers with a collective).  Other
+    errors raise."""
+    L = nat.lib()
+    _check_device(w, x2d)
+    dev = x2d.device
+    M = x2d.shape[0]
+    r = 0 if A is None else A.shape[0]
+    with torch.cuda.device(dev):
+        nbytes = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
+        ws = nat.workspace(dev, nbytes)
+        rc = L.rq_linear_forward_gather(*w.args(), x2d.data_ptr(), nat.dtype_code(x2d.dtype), M, nat.ptr(bias),
+                                        nat.dtype_code(bias.dtype) if bias is not None else 0, nat.ptr(A), nat.ptr(B),
+                                        r, float(scaling), ctypes.byref(gather), ws.data_ptr(), ws.numel(),
+                                        nat.stream_ptr(dev))
+    if rc != nat.RQ_ERR_UNSUPPORTED:
+        nat.check(rc, "rq_linear_forward_gather")
+    return rc
 
 
 def dx(w: WeightView, dy2d: torch.Tensor, A: Optional[torch.Tensor], B: Optional[torch.Tensor],

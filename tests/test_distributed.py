@@ -72,8 +72,10 @@ def _rank_main(rank, world, port, N, K, M, r):
         ref(x_ref).backward(dY)
 
         lo, hi = shard_range(N, world, rank)
-        layer = ColumnParallelLinear(_TorchLoRAShard(W[lo:hi], A, B[lo:hi], 2.0), N)
-        assert (layer.lo, layer.hi) == (lo, hi)
+        # gather_tokens asks for the fused NVLink gather; without NCCL (gloo)
+        # the layer keeps the collective path
+        layer = ColumnParallelLinear(_TorchLoRAShard(W[lo:hi], A, B[lo:hi], 2.0), N, gather_tokens=16)
+        assert (layer.lo, layer.hi) == (lo, hi) and layer.peer is None
         x = X.clone().requires_grad_(True)
         y = layer(x)
         torch.testing.assert_close(y, ref(X), rtol=1e-5, atol=1e-4)

@@ -1,0 +1,127 @@
+"""Two-rank GPU tests of the column-sharded layer with the fused gather:
+the decode GEMV writes each rank's output features into every rank's full
+output over NVLink (rocm_qlora.distributed.peer_gather).
+
+The gathered output must equal, bit for bit, (a) the NCCL all-gather path of
+the same sharded layer and (b) the unsharded layer on one GPU: with K a
+multiple of 64 the shards quantize to the same codes and scales as the
+full weight's rows, and the GEMV's per-row reduction order does not depend
+on the shard.  Needs two GPUs (one process per GPU, NCCL over 127.0.0.1);
+skipped otherwise."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # full out_features, K, M, LoRA r, bias
+    (4096, 4096, 1, 16, False),
+    (22016, 4096, 16, 16, False),   # 2 x 11008
+    (1000, 1024, 4, 0, True),       # uneven shards (496 / 504 rows), no adapter
+    (4096, 11008, 8, 16, True),     # K not a multiple of 256
+]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, q) -> None:
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "rocm-qlora_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+    import torch.nn as nn
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    ok = False
+    try:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        from rocm_qlora import LoRALinear, QuantLinear
+        from rocm_qlora import _native as nat
+        from rocm_qlora.distributed import ColumnParallelLinear
+        import ctypes
+        msgs = []
+        for (Nt, K, M, r, bias) in CASES:
+            g = torch.Generator().manual_seed(Nt + K + M + r)
+            W = (torch.randn(Nt, K, generator=g) * 0.02).to(torch.bfloat16)
+            bvec = (torch.randn(Nt, generator=g) * 0.1).to(torch.bfloat16) if bias else None
+            A = (torch.rand(max(r, 1), K, generator=g) * 2 - 1) / K ** 0.5
+            B = torch.randn(Nt, max(r, 1), generator=g) * 0.01
+            X = torch.randn(M, K, generator=g).to(torch.bfloat16)
+            lin = nn.Linear(K, Nt, bias=bias, dtype=torch.bfloat16, device=dev)
+            with torch.no_grad():
+                lin.weight.copy_(W.to(dev))
+                if bias:
+                    lin.bias.copy_(bvec.to(dev))
+            cp = ColumnParallelLinear.from_linear(lin, bits=4, double_quant=True, lora_r=r, lora_alpha=2 * max(r, 1),
+                                                  gather_tokens=16)
+            assert cp.peer is not None
+            if r:
+                with torch.no_grad():
+                    cp.local.lora_A.copy_(A.to(dev))
+                    cp.local.lora_B.copy_(B[cp.lo:cp.hi].to(dev))
+            cp.eval()
+            x = X.to(dev)
+            with torch.no_grad():
+                y_fused = cp(x).clone()
+                assert nat.lib().rq_last_path() == 1  # the decode GEMV ran
+                peer, cp.peer = cp.peer, None
+                y_nccl = cp(x)
+                cp.peer = peer
+            assert not peer.error(), "a rank gave up waiting for a peer"
+            c = ctypes.c_uint(0)
+            assert nat.lib().rq_take_kernel_timeouts(ctypes.byref(c)) == 0 and c.value == 0
+            assert torch.equal(y_fused, y_nccl), f"fused != NCCL for {(Nt, K, M, r, bias)}"
+            # the unsharded layer on this GPU
+            ql = QuantLinear.from_linear(lin, bits=4)
+            ql.enable_double_quant()
+            full = LoRALinear(ql, r=r, lora_alpha=2 * r).to(dev).eval() if r else ql
+            if r:
+                with torch.no_grad():
+                    full.lora_A.copy_(A.to(dev))
+                    full.lora_B.copy_(B.to(dev))
+            with torch.no_grad():
+                y_full = full(x)
+            assert torch.equal(y_fused, y_full), f"fused != unsharded for {(Nt, K, M, r, bias)}"
+            cp.close()
+            msgs.append(f"{(Nt, K, M, r, bias)} ok")
+        ok = True
+        q.put((rank, "ok", msgs))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e), []))
+    finally:
+        if dist.is_initialized():
+            if ok:
+                dist.barrier()
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_gather_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in procs:
+        results.append(q.get(timeout=600))
+    for p in procs:
+        p.join(timeout=120)
+    for rank, status, msgs in results:
+        assert status == "ok", f"rank {rank}: {status}"
+        assert len(msgs) == len(CASES)
