@@ -76,13 +76,17 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// The end of a gathering call, run by one thread of every CTA after the
-// CTA's stores are fenced at system scope.  The last CTA of this rank to
-// arrive (all of the rank's stores are then issued and fenced) advances the
-// epoch, publishes it in every rank's flag slot for this rank (release at
-// system scope) and waits, at most about 2 s, until every rank's flag here
-// holds the epoch: from then on every rank's shard of this call is in this
-// rank's Y.  The arrival counter goes back to zero for the next call.
+// The end of a gathering call, run by one thread of every CTA after a CTA
+// barrier has ordered the CTA's stores before it.  Each CTA arrives with an
+// acquire-release atomic (GPU scope); the last CTA to arrive has thereby
+// acquired every CTA's stores.  It advances the epoch and publishes it in
+// every rank's flag slot for this rank with a release at system scope
+// (cumulative: the rank's stores to all ranks' Y are visible before the
+// flag), then waits, at most about 2 s, until every rank's flag here holds
+// the epoch (acquire at system scope): from then on every rank's shard of
+// this call is in this rank's Y.  One system-scope release per call is the
+// whole fence cost (a system fence in every CTA cost ~5 us a call).  The
+// arrival counter goes back to zero for the next call.
 __device__ void gather_arrive(const RqGather& g) {
   uint32_t* ctrl = g.ctrl;
   uint32_t arrived;
@@ -91,7 +95,6 @@ __device__ void gather_arrive(const RqGather& g) {
   ctrl[0] = 0;
   const uint32_t epoch = ctrl[1] + 1;
   ctrl[1] = epoch;
-  __threadfence_system();
   for (int q = 0; q < g.world; ++q) {
     uint32_t* f = g.flags[q] + g.rank;
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
@@ -131,6 +134,7 @@ struct Nf4Args {
   uint32_t raw_off;     //   raw scale bytes of a pass, c2_scales of a pass,
   uint32_t aux_off;     //   256-entry second-level scale table,
   uint32_t tl_off;      //   staged x.A^T
+  uint32_t stg_off;     //   a pass's outputs [M][NT*16] (gathering calls)
 };
 
 // NF4 level c (the values of kNF4) from immediates: no memory access, so the
@@ -333,6 +337,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   float* sc = reinterpret_cast<float*>(smem + q.sc_off);
   float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
   T* tl = reinterpret_cast<T*>(smem + q.tl_off);
+  T* stg = reinterpret_cast<T*>(smem + q.stg_off);
   const uint32_t lanesel = sbase + (uint32_t)(lane * 4);
   // lane's code bytes in a slot: logical 16-byte chunk 2*(warp & 3) + (t >> 1)
   // of 128-byte half warp >> 2 of tile row mma_row(g) (+16 nt + 8 h), half t & 1;
@@ -513,11 +518,30 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       }
       const float bv = has_bias ? load_scalar(p.bias, p.bdt, row) : 0.0f;
       const T v = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, uu, has_lora, p.s));
-      if (p.gather) {  // into every rank's Y[:, col + row] (NVLink stores to the peers)
-        const size_t o = (size_t)m * p.gth.ld + p.gth.col + row;
-        for (int rq = 0; rq < p.gth.world; ++rq) static_cast<T*>(p.gth.outs[rq])[o] = v;
-      } else {
+      if (p.gather)
+        stg[m * (NT * 16) + rl] = v;
+      else
         y[(size_t)m * N + row] = v;
+    }
+    if (p.gather) {
+      // the pass's outputs into every rank's Y[:, col + c0 ...]: 16-byte row
+      // pieces where the destinations are 16-byte aligned (one NVLink write
+      // each), the rest element by element
+      consumer_sync();
+      const int64_t ld = p.gth.ld, col0 = p.gth.col + c0;
+      const int R8 = ((ld | col0) & 7) == 0 ? (R & ~7) : 0, nb8 = R8 / 8;
+      for (int i = tid; i < M * nb8; i += kNfThreads) {
+        const int m = i / nb8, j = (i - m * nb8) * 8;
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + m * (NT * 16) + j);
+        const size_t o = (size_t)m * ld + col0 + j;
+        for (int rq = 0; rq < p.gth.world; ++rq) *reinterpret_cast<uint4*>(static_cast<T*>(p.gth.outs[rq]) + o) = v;
+      }
+      const int rest = R - R8;
+      for (int i = tid; i < M * rest; i += kNfThreads) {
+        const int m = i / rest, j = R8 + (i - m * rest);
+        const T v = stg[m * (NT * 16) + j];
+        const size_t o = (size_t)m * ld + col0 + j;
+        for (int rq = 0; rq < p.gth.world; ++rq) static_cast<T*>(p.gth.outs[rq])[o] = v;
       }
     }
     consumer_sync();  // partial sums (and per-pass scales) are reused by the next pass
@@ -537,7 +561,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       }
   }
   if (p.gather) {
-    __threadfence_system();  // this thread's stores to the ranks' Y, before the CTA's arrival
+    // every consumer's stores of the call are ordered before the arrival by
+    // the barrier; the arrival's release covers them
     consumer_sync();
     if (tid == 0) gather_arrive(p.gth);
   }
@@ -617,12 +642,12 @@ int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64
 struct Nf4Plan {
   int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
   size_t smem;
-  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off;
+  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off;
 };
 
 // [code table | scales | raw scales + c2_scales of a pass | second-level
-// table | x.A^T | ring (1 KB aligned) | partial sums]; with one pass the
-// partial sums reuse the ring.
+// table | x.A^T | staged outputs | ring (1 KB aligned) | partial sums];
+// with one pass the partial sums reuse the ring.
 static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
   size_t off = kLutBytes;
@@ -634,6 +659,8 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   off += 1024;
   pl->tl_off = (uint32_t)off;
   off += align16((size_t)M * (r > 0 ? r : 0) * 2);
+  pl->stg_off = (uint32_t)off;
+  off += align16((size_t)M * pl->nt * 16 * 2);
   pl->ring_off = (uint32_t)off;
   off += 1024;  // room to round the ring up to a 1 KB shared address
   const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)kNfWarps * pl->nt * pl->mg * 512;
@@ -761,6 +788,7 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   q.raw_off = pl.raw_off;
   q.aux_off = pl.aux_off;
   q.tl_off = pl.tl_off;
+  q.stg_off = pl.stg_off;
   if (g.xdt == RQ_BF16)
     return pl.mg == 2 ? nf4_nt<RQ_BF16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_BF16, 1>(q, pl.nt, pl.smem, pdl, st);
   return pl.mg == 2 ? nf4_nt<RQ_F16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_F16, 1>(q, pl.nt, pl.smem, pdl, st);
