@@ -173,14 +173,25 @@ def run_ours(args, rank, world, device):
 
     gather_out, peers = {}, {}
     fused = world > 1 and args.gather == "fused"
-    if world > 1:
+    if fused:
+        # the shared output buffers; if any rank cannot set them up, every
+        # rank gathers with NCCL instead (the ranks must take the same path)
         from rocm_qlora.distributed.peer_gather import PeerGather
+        ok = 1
+        try:
+            for si, (N, K) in enumerate(SHAPES):
+                for M in MS:  # this rank's N columns of the full [M, world*N] output, on every rank
+                    peers[(si, M)] = PeerGather(None, M, world * N, rank * N, torch.bfloat16, device)
+        except Exception as e:  # reported in the JSON line
+            ok = 0
+            print(f"rank {rank}: fused gather unavailable ({e!r}); using NCCL", file=sys.stderr, flush=True)
+        t = torch.tensor([ok], device=device, dtype=torch.int32)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        fused = bool(t.item())
+    if world > 1 and not fused:
         for si, (N, K) in enumerate(SHAPES):
             for M in MS:
-                if fused:  # this rank's N columns of the full [M, world*N] output, on every rank
-                    peers[(si, M)] = PeerGather(None, M, world * N, rank * N, torch.bfloat16, device)
-                else:
-                    gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
+                gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
 
     def step(c, lora=True):
         """One sweep pass.  lora=True is the measured step (adapter, and the

@@ -689,6 +689,177 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TL::kTmemCols) : "memory");
 }
 
+
+// ------------------------------------------------------------------------
+// LoRA down product of the prefill / training paths on the tensor cores:
+//   forward  t  = rnd(X[M, Kr] . A^T)          A  [R, Kr] (K-major operand)
+//   dX       gt = rnd(s . (dY[M, Kr] . B))      B  [Kr, R] (MN-major operand)
+// (dX only for s a power of two: then rnd(dY*s) = dY*s exactly and scaling
+// the fp32 sum is exact, so this equals the reference's rnd(rnd(dY*s).B)).
+// A cluster of SK CTAs shares a 128-row tile, CTA k reducing the k-th slice
+// of the 64-wide steps; each accumulates in tensor memory (M=128, N=RP),
+// parks its fp32 partial in shared memory, and the cluster's rank 0 sums
+// the partials in rank order through distributed shared memory (fixed
+// order: deterministic), rounds and stores.  6 warps: TMA producer, MMA
+// issuer (+ tensor memory), 4 epilogue warps (one TMEM lane quarter each).
+constexpr int kLdStages = 3;
+constexpr int kLdThreads = 192;
+constexpr uint32_t kLdX = 128 * 64 * 2;   // X tile, 16 KB
+constexpr uint32_t kLdW = 64 * 64 * 2;    // A / B tile, 8 KB (rows past R zero-filled)
+constexpr int kLdRedStride = 64 + 4;      // floats a row of the parked partial (bank spread)
+constexpr uint32_t kLdSmem = kLdStages * (kLdX + kLdW) + 128 * kLdRedStride * 4 + 1024;
+
+struct LoraDownArgs {
+  CUtensorMap xmap;   // X / dY [M][Kr], box 64 x 128, 128-byte swizzle
+  CUtensorMap wmap;   // A [R][Kr] box 64 x RP (forward), B [Kr][R] box 64 x 64 (dX), 128-byte swizzle
+  void* out;          // [M][R] activation dtype
+  int M, Kr, R, rp, sk;
+  float s;            // dX scale (a power of two), 1 forward
+};
+
+template <int DT, bool WT>
+__global__ void __launch_bounds__(kLdThreads, 1) lora_down_tc_k(const __grid_constant__ LoraDownArgs g) {
+  using T = typename DType<DT>::T;
+  extern __shared__ __align__(1024) unsigned char dsm[];
+  __shared__ __align__(8) uint64_t bars[2 * kLdStages + 1];  // full[S], empty[S], acc
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag, issued, consumed;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t sraw = smem_u32(dsm), sbase = (sraw + 1023u) & ~1023u;
+  unsigned char* sm = dsm + (sbase - sraw);
+  float* red = reinterpret_cast<float*>(sm + kLdStages * (kLdX + kLdW));
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * kLdStages, accbar = empty0 + 8 * kLdStages;
+  // waits give up on this CTA's flag only (the cluster meets at barriers the
+  // whole cluster always reaches)
+  const Abort ab{&abort_flag, mapa(smem_u32(&abort_flag), rank)};
+  const int m0 = (int)(blockIdx.x / g.sk) * 128;
+  const int nsteps = g.Kr / 64;
+  const int s0 = nsteps * (int)rank / g.sk, s1 = nsteps * ((int)rank + 1) / g.sk;
+  const uint32_t tcols = g.rp <= 32 ? 32u : 64u;
+
+  if (tid == 0) {
+    for (int i = 0; i < kLdStages; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, 1);
+    }
+    mbar_init(accbar, 1);
+    abort_flag = 0;
+    issued = 0;
+    consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(tcols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int st = s0; st < s1; ++st) {
+        const int i = st - s0, slot = i % kLdStages;
+        if (i >= kLdStages && !mbar_wait(empty0 + 8 * slot, ((i / kLdStages) - 1) & 1, ab)) break;
+        const uint32_t xs = sbase + slot * (kLdX + kLdW), ws = xs + kLdX;
+        mbar_expect_tx(full0 + 8 * slot, kLdX + (WT ? kLdW : (uint32_t)g.rp * 128));
+        tma_2d(xs, &g.xmap, st * 64, m0, full0 + 8 * slot);
+        if (WT)
+          tma_2d(ws, &g.wmap, 0, st * 64, full0 + 8 * slot);
+        else
+          tma_2d(ws, &g.wmap, st * 64, 0, full0 + 8 * slot);
+        *reinterpret_cast<volatile int*>(&issued) = i + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t ab16 = DT == RQ_BF16 ? 1u : 0u;
+      const uint32_t idesc = (1u << 4) | (ab16 << 7) | (ab16 << 10) | ((WT ? 1u : 0u) << 16) |
+                             ((uint32_t)(g.rp >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      for (int st = s0; st < s1; ++st) {
+        const int i = st - s0, slot = i % kLdStages;
+        if (!mbar_wait(full0 + 8 * slot, (i / kLdStages) & 1, ab)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t xs = sbase + slot * (kLdX + kLdW), ws = xs + kLdX;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t db = WT ? sw128_mn_desc(ws + kk * 2048, 8192) : sw128_desc(ws + kk * 32);
+          asm volatile(
+              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+              " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+              "l"(sw128_desc(xs + kk * 32)), "l"(db), "r"(idesc), "r"((i > 0 || kk > 0) ? 1u : 0u)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(empty0 +
+                                                                                                      8 * slot)
+                     : "memory");
+        *reinterpret_cast<volatile int*>(&consumed) = i + 1;
+      }
+      // all of this CTA's MMAs (none when its slice is empty) are complete
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(accbar)
+                   : "memory");
+    }
+  } else {
+    // ---------------------------------------------- epilogue warps (2..5)
+    const int quad = warp & 3, row = quad * 32 + lane;
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait(accbar, 0, ab) && !ab.raised();
+    ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    float* myrow = red + row * kLdRedStride;
+    for (int c = 0; c < g.rp; c += 32) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c + j < 64) myrow[c + j] = (ok && s1 > s0) ? v[j] : 0.0f;
+    }
+  }
+  // the partials are parked: rank 0 sums them in rank order
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  cluster_sync();
+  if (rank == 0 && warp >= 2) {
+    const int quad = warp & 3, row = quad * 32 + lane, m = m0 + row;
+    const uint32_t mine = smem_u32(red + row * kLdRedStride);
+    T* out = static_cast<T*>(g.out);
+    for (int c = 0; c < g.R; c += 4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < g.sk; ++q) {
+        float4 v;
+        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                     : "r"(mapa(mine + c * 4, (uint32_t)q)));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      if (m < g.M) {
+        const float o[4] = {acc.x * g.s, acc.y * g.s, acc.z * g.s, acc.w * g.s};
+        for (int j = 0; j < 4 && c + j < g.R; ++j) out[(size_t)m * g.R + c + j] = DType<DT>::from_f32(o[j]);
+      }
+    }
+  }
+  // peers stay alive until rank 0 has read their partials; drain after an abort
+  __syncwarp();
+  cluster_sync();
+  if (warp == 1 && lane == 0 && ab.raised()) {
+    mbar_drain(accbar, 0);
+    const int done = *reinterpret_cast<volatile int*>(&consumed), n = *reinterpret_cast<volatile int*>(&issued);
+    for (int i = done; i < n; ++i) mbar_drain(full0 + 8 * (i % kLdStages), (i / kLdStages) & 1);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- host side
@@ -792,6 +963,80 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
 }
 
 int gemm_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) { return gemm_launch(a, false, a.x, tdown, st); }
+
+// The tensor-core down product for M >= 256 (see lora_down_tc_k); returns
+// RQ_ERR_UNSUPPORTED (nothing launched) for arguments it does not take, and
+// the caller runs lora_down instead.
+int lora_down_tc(int dt, bool wt, const void* X, int64_t M, int64_t Kr, const void* W2, int R, float pre_s,
+                 bool do_pre, void* out, cudaStream_t st) {
+  if ((dt != RQ_BF16 && dt != RQ_F16) || M < 256 || M > 0x7fffffff || R < 8 || R > 64 || R % 8 || Kr % 64 ||
+      Kr > 0x7fffffff)
+    return RQ_ERR_UNSUPPORTED;
+  float s = 1.0f;
+  if (do_pre) {  // exact only for a power-of-two scale
+    int e = 0;
+    if (!(pre_s > 0.0f) || frexpf(pre_s, &e) != 0.5f) return RQ_ERR_UNSUPPORTED;
+    s = pre_s;
+  }
+  if ((uintptr_t)X % 16 || (uintptr_t)W2 % 16 || (uintptr_t)out % 4) return RQ_ERR_UNSUPPORTED;
+  LoraDownArgs g;
+  const int ty = CU_TENSOR_MAP_DATA_TYPE_UINT16, swz = CU_TENSOR_MAP_SWIZZLE_128B;
+  const int rp = (R + 15) / 16 * 16;
+  {
+    const uint64_t d[3] = {(uint64_t)Kr, (uint64_t)M, 1}, sd[2] = {(uint64_t)Kr * 2, 0};
+    const uint32_t b[3] = {64, 128, 1};
+    const int rc = tensor_map_encode(ty, swz, 2, X, d, sd, b, &g.xmap);
+    if (rc != RQ_OK) return rc;
+  }
+  {
+    int rc;
+    if (wt) {  // B [Kr][R]: 64 K rows x 64 columns (past R zero-filled), MN-major operand
+      const uint64_t d[3] = {(uint64_t)R, (uint64_t)Kr, 1}, sd[2] = {(uint64_t)R * 2, 0};
+      const uint32_t b[3] = {64, 64, 1};
+      rc = tensor_map_encode(ty, swz, 2, W2, d, sd, b, &g.wmap);
+    } else {  // A [R][Kr]: rp rows (past R zero-filled) x 64 K
+      const uint64_t d[3] = {(uint64_t)Kr, (uint64_t)R, 1}, sd[2] = {(uint64_t)Kr * 2, 0};
+      const uint32_t b[3] = {64, (uint32_t)rp, 1};
+      rc = tensor_map_encode(ty, swz, 2, W2, d, sd, b, &g.wmap);
+    }
+    if (rc != RQ_OK) return rc;
+  }
+  const int64_t tiles = (M + 127) / 128, nsteps = Kr / 64;
+  int64_t sk = (2 * (int64_t)num_sms() + tiles - 1) / tiles;
+  if (sk > 8) sk = 8;
+  if (sk > nsteps) sk = nsteps;
+  if (sk < 1) sk = 1;
+  g.out = out;
+  g.M = (int)M;
+  g.Kr = (int)Kr;
+  g.R = R;
+  g.rp = rp;
+  g.sk = (int)sk;
+  g.s = s;
+  const void* kern = dt == RQ_BF16 ? (wt ? (const void*)lora_down_tc_k<RQ_BF16, true> : (const void*)lora_down_tc_k<RQ_BF16, false>)
+                                   : (wt ? (const void*)lora_down_tc_k<RQ_F16, true> : (const void*)lora_down_tc_k<RQ_F16, false>);
+  int rc = ensure_smem_limit(kern, kLdSmem);
+  if (rc != RQ_OK) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles * sk), 1, 1);
+  cfg.blockDim = dim3(kLdThreads, 1, 1);
+  cfg.dynamicSmemBytes = kLdSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)sk;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  void* args[] = {&g};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return RQ_ERR_CUDA;
+  }
+  return check_launch();
+}
 
 // dX: a.x is dY [M][N], gt = rnd(rnd(dY*s).B) [M][r], a.y the dX output.
 int gemm_dx(const LinearArgs& a, const void* gt, cudaStream_t st) {

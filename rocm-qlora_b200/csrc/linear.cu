@@ -19,6 +19,13 @@ namespace rq {
 bool gemm_supported(const LinearArgs& a, bool dx);
 int gemm_forward(const LinearArgs& a, const void* tdown, cudaStream_t st);
 int gemm_dx(const LinearArgs& a, const void* gt, cudaStream_t st);
+int lora_down_tc(int dt, bool wt, const void* X, int64_t M, int64_t Kr, const void* W2, int R, float pre_s,
+                 bool do_pre, void* out, cudaStream_t st);
+
+// The LoRA down product: on the tensor cores for prefill-sized M where it
+// applies (gemm_tcgen05.cu), else the mma.sync / CUDA-core kernels.
+static int lora_down_any(const LinearArgs& a, bool wt, const void* X, int64_t Kr, const void* W2, float pre_s,
+                         bool do_pre, const struct WsView& v, cudaStream_t st);
 
 static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
@@ -42,6 +49,14 @@ struct WsView {
   float* partial;
   int64_t partial_elems;
 };
+
+static int lora_down_any(const LinearArgs& a, bool wt, const void* X, int64_t Kr, const void* W2, float pre_s,
+                         bool do_pre, const WsView& v, cudaStream_t st) {
+  const int rc = lora_down_tc(a.xdt, wt, X, a.M, Kr, W2, a.r, pre_s, do_pre, v.t, st);
+  if (rc != RQ_ERR_UNSUPPORTED) return rc;
+  return lora_down(a.xdt, wt, X, a.M, Kr, W2, a.r, pre_s, do_pre, v.t, v.partial, v.partial_elems, v.counters, 64,
+                   st);
+}
 
 static int carve(const LinearArgs& a, WsView* v) {
   v->counters = nullptr;
@@ -93,8 +108,7 @@ int linear_forward(const LinearArgs& a, cudaStream_t st) {
   if (rc != RQ_OK) return rc;
   if (a.M == 0 || a.w.N == 0) return RQ_OK;
   if (a.r > 0) {
-    rc = lora_down(a.xdt, false, a.lora_x, a.M, a.w.K, a.lora_a, a.r, 1.0f, false, v.t, v.partial, v.partial_elems,
-                   v.counters, 64, st);
+    rc = lora_down_any(a, false, a.lora_x, a.w.K, a.lora_a, 1.0f, false, v, st);
     if (rc != RQ_OK) return rc;
   }
   LinearArgs g = a;
@@ -123,8 +137,7 @@ int linear_dx(const LinearArgs& a, cudaStream_t st) {
   if (a.M == 0 || a.w.K == 0) return RQ_OK;
   if (a.r > 0) {
     // gt = rnd(rnd(dy * s) . B): B is [N, r], the reduction runs over N
-    rc = lora_down(a.xdt, true, a.x, a.M, a.w.N, a.lora_b, a.r, a.scaling, true, v.t, v.partial, v.partial_elems,
-                   v.counters, 64, st);
+    rc = lora_down_any(a, true, a.x, a.w.N, a.lora_b, a.scaling, true, v, st);
     if (rc != RQ_OK) return rc;
   }
   if (gemm_supported(a, true)) {

@@ -60,21 +60,40 @@ class PeerGather:
         typestr, esz = _TYPESTR[dtype]
         self._own: List[int] = []
         self._opened: List[int] = []
+        # Every rank takes part in both exchanges whatever happens locally,
+        # and all ranks raise together if any rank failed: the group's
+        # collectives stay matched.
         with torch.cuda.device(self.device):
-            out = self._alloc(L, max_tokens * out_features * esz)
-            flags = self._alloc(L, 4 * self.world)
-            self._ctrl = self._alloc(L, 16)
-            handles = (self._handle(L, out), self._handle(L, flags))
+            handles, err = None, None
+            try:
+                out = self._alloc(L, max_tokens * out_features * esz)
+                flags = self._alloc(L, 4 * self.world)
+                self._ctrl = self._alloc(L, 16)
+                handles = (self._handle(L, out), self._handle(L, flags))
+            except Exception as e:
+                err = e
             every = [None] * self.world
             dist.all_gather_object(every, handles, group=group)
             outs, fl = [], []
-            for q, (ho, hf) in enumerate(every):
-                if q == self.rank:
-                    outs.append(out)
-                    fl.append(flags)
-                else:
-                    outs.append(self._open(L, ho))
-                    fl.append(self._open(L, hf))
+            if err is None and all(h is not None for h in every):
+                try:
+                    for q, (ho, hf) in enumerate(every):
+                        if q == self.rank:
+                            outs.append(out)
+                            fl.append(flags)
+                        else:
+                            outs.append(self._open(L, ho))
+                            fl.append(self._open(L, hf))
+                except Exception as e:
+                    err = e
+            else:
+                err = err or RuntimeError("another rank could not allocate its shared buffers")
+            verdict = [None] * self.world
+            dist.all_gather_object(verdict, err is None, group=group)
+            if not all(verdict):
+                self._release_local(L)
+                raise RuntimeError(f"fused gather unavailable on this node: {err!r}" if err is not None
+                                   else "fused gather unavailable: another rank failed to map the buffers")
             self._outs_dev = torch.tensor(outs, dtype=torch.int64, device=self.device)
             self._flags_dev = torch.tensor(fl, dtype=torch.int64, device=self.device)
             self.y = torch.as_tensor(_DeviceArray(out, (max_tokens, out_features), typestr),
@@ -105,6 +124,13 @@ class PeerGather:
         nat.check(L.rq_peer_open(handle, ctypes.byref(p)), "rq_peer_open")
         self._opened.append(p.value)
         return p.value
+
+    def _release_local(self, L) -> None:
+        for p in self._opened:
+            L.rq_peer_close(p)
+        for p in self._own:
+            L.rq_peer_free(p)
+        self._own, self._opened = None, []
 
     def output(self, M: int) -> torch.Tensor:
         """Y[:M] of the last gathering call (a view of the shared buffer)."""

@@ -104,3 +104,24 @@ def test_prefill_matches_decode_slabs_bitwise_free_of_state():
         y1 = lora(x).float().cpu().numpy()
         y2 = lora(x).float().cpu().numpy()
     assert np.array_equal(y1, y2)
+
+
+@pytest.mark.parametrize("M", [300, 2048])
+def test_prefill_dx_non_power_of_two_scaling(M):
+    """dX with scaling 1.5: the tensor-core down product takes only power-of-
+    two scales (exactness), so the other kernel computes gt = rnd(rnd(dY*s).B);
+    the result stays within the tolerance of the reference."""
+    from rocm_qlora import _native as nat
+    N, K, r = 1024, 2048, 16
+    inp = layer_inputs(N, K, M, sigma=0.02, r=r, alpha=24, w_dtype=torch.bfloat16, x_dtype=torch.bfloat16,
+                       seed=M + 5, with_dy=True)
+    lora = build_layer(inp.W, 4, True, None, r, 24, inp.A, inp.B)
+    assert lora.scaling == 1.5
+    x = inp.X.cuda().requires_grad_(True)
+    lora(x).backward(inp.dY.cuda())
+    torch.cuda.synchronize()
+    assert nat.lib().rq_last_path() == RQ_PATH_GEMM
+    assert ctypes_count(nat) == 0
+    wdeq = oracle_wdeq(lora.base_layer, N, K)
+    dx_ref = orc.loralinear_dx(to_f32(inp.dY), wdeq, inp.A.numpy(), inp.B.numpy(), lora.scaling, DTC[torch.bfloat16])
+    assert_matmul_close(to_f32(x.grad), dx_ref, DTC[torch.bfloat16], roundings=2)
