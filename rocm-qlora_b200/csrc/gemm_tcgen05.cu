@@ -95,13 +95,15 @@ template <int BN>
 struct Tile {
   static constexpr int BNH = BN / 2;                  // weight rows (dX: output columns) a CTA
   static constexpr uint32_t kBBytes = BNH * BK * 2;   // 16 KB / 8 KB
-  static constexpr uint32_t kStage = kABytes + kBBytes;
+  static constexpr uint32_t kCBytes = BNH * 32;       // forward: this CTA's code bytes of one stage (4 / 2 KB)
+  static constexpr uint32_t kStage = kABytes + kBBytes + kCBytes;
   static constexpr uint32_t kFixed = kABytes + kBBytes + kLutBytes + 1024 + 1024;  // LoRA tiles, LUT, sclut, align
   static constexpr int kFit = (int)((kSmemCap - kFixed) / kStage);
   static constexpr int kStages = kFit > 6 ? 6 : kFit;
   static constexpr uint32_t kSmA = 0;                               // kStages x 16 KB
   static constexpr uint32_t kSmB = kSmA + kStages * kABytes;        // kStages x kBBytes
-  static constexpr uint32_t kSmT = kSmB + kStages * kBBytes;        // LoRA t (gt) tile, 16 KB
+  static constexpr uint32_t kSmC = kSmB + kStages * kBBytes;        // kStages x kCBytes (codes by TMA)
+  static constexpr uint32_t kSmT = kSmC + kStages * kCBytes;        // LoRA t (gt) tile, 16 KB
   static constexpr uint32_t kSmLB = kSmT + kABytes;                 // LoRA B (dX: A) tile
   static constexpr uint32_t kSmLut = kSmLB + kBBytes;               // code byte -> (T[lo], T[hi])
   static constexpr uint32_t kSmScl = kSmLut + kLutBytes;            // 256 fp32 second-level values
@@ -115,6 +117,7 @@ struct GemmArgs {
   CUtensorMap xmap;   // X [M][K] (dX: dY [M][N]), box 64 x 128, 128-byte swizzle
   CUtensorMap tmap;   // t [M][r] (dX: gt), box 64 x 128, 128-byte swizzle (r < 64 zero-filled)
   CUtensorMap bmap;   // LoRA B [N][r], box 64 x BN/2 (dX: A [r][K], box 64 x 64), 128-byte swizzle
+  CUtensorMap cmap;   // forward: codes uint8 [N][K/2], box 32 x BN/2 (one stage of this CTA's rows)
   QWeight w;
   const void* bias;
   int bdt;
@@ -286,6 +289,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 32-column loads (base and LoRA accumulators of the same rows) under
+// one wait: one tensor-memory round trip instead of two.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
+  uint32_t ra[32], rb[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(ra[0]), "=r"(ra[1]), "=r"(ra[2]), "=r"(ra[3]), "=r"(ra[4]), "=r"(ra[5]), "=r"(ra[6]), "=r"(ra[7]), "=r"(ra[8]), "=r"(ra[9]), "=r"(ra[10]), "=r"(ra[11]), "=r"(ra[12]), "=r"(ra[13]), "=r"(ra[14]), "=r"(ra[15]), "=r"(ra[16]), "=r"(ra[17]), "=r"(ra[18]), "=r"(ra[19]), "=r"(ra[20]), "=r"(ra[21]), "=r"(ra[22]), "=r"(ra[23]), "=r"(ra[24]), "=r"(ra[25]), "=r"(ra[26]), "=r"(ra[27]), "=r"(ra[28]), "=r"(ra[29]), "=r"(ra[30]), "=r"(ra[31]), "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]), "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]), "=r"(rb[14]), "=r"(rb[15]), "=r"(rb[16]), "=r"(rb[17]), "=r"(rb[18]), "=r"(rb[19]), "=r"(rb[20]), "=r"(rb[21]), "=r"(rb[22]), "=r"(rb[23]), "=r"(rb[24]), "=r"(rb[25]), "=r"(rb[26]), "=r"(rb[27]), "=r"(rb[28]), "=r"(rb[29]), "=r"(rb[30]), "=r"(rb[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    a[i] = __uint_as_float(ra[i]);
+    b[i] = __uint_as_float(rb[i]);
+  }
+}
+
 // Read-only global loads pinned where they are written (volatile asm): the
 // dequant warps' prefetch of codes and scales must be issued stages ahead
 // of its use, not sunk to it by the compiler.
@@ -419,8 +440,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         const int slot = kb % S;
         if (kb >= S && !mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab)) break;
         if (rank == 0) mbar_expect_tx(fullB0 + 8 * slot, 16);  // the peer's "stage ready" signal
-        mbar_expect_tx(fullA0 + 8 * slot, kABytes);
+        mbar_expect_tx(fullA0 + 8 * slot, kABytes + (DX ? 0u : TL::kCBytes));
         tma_2d(sbase + TL::kSmA + slot * kABytes, &g.xmap, kb * BK, m0, fullA0 + 8 * slot);
+        if (!DX) tma_2d(sbase + TL::kSmC + slot * TL::kCBytes, &g.cmap, kb * 32, nh0, fullA0 + 8 * slot);
         *reinterpret_cast<volatile int*>(&a_issued) = kb + 1;
       }
     }
@@ -517,20 +539,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         const int blk = DX ? (nh0 >> 6) + dq : kb;
         if (DX ? (dx_active && blk < nbk) : n < N) {
           const uint8_t* src = qb + (size_t)n * (K / 2) + (size_t)blk * 32;
-          if (DX) {
+          if (DX) {  // forward codes arrive by TMA with the stage
             const uint2 v = ldg_pin2(reinterpret_cast<const uint2*>(src) + dpart);
             r.c[2 * h] = v.x;
             r.c[2 * h + 1] = v.y;
-          } else if (CW == 4) {
-            const uint4 v = ldg_pin4(reinterpret_cast<const uint4*>(src) + fpart);
-            r.c[0] = v.x;
-            r.c[1] = v.y;
-            r.c[2] = v.z;
-            r.c[3] = v.w;
-          } else {
-            const uint2 v = ldg_pin2(reinterpret_cast<const uint2*>(src) + fpart);
-            r.c[0] = v.x;
-            r.c[1] = v.y;
           }
           const int64_t bi = (int64_t)n * nbk + blk;
           if (fmt == RQ_W_NF4) {
@@ -542,16 +554,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         }
       }
     };
-    auto convert = [&](int kb, const Raw& r) -> bool {
+    // sv0 / sv1: the block scales of the stage (forward: sv0 of this row;
+    // dX: of weight rows 64 kb + 2p and +1); r: dX codes
+    auto convert = [&](int kb, const Raw& r, float sv0, float sv1) -> bool {
       const int slot = kb % S;
-      float sv[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) sv[h] = fmt == RQ_W_NF4 ? r.sraw[h] : sclut[r.c2b[h]] * r.sraw[h];
+      const float sv[2] = {sv0, sv1};
       // lane 0 polls the barrier (the other lanes wait in the shuffle, so
       // the shared-memory pipe the TMA writes through is not flooded with
       // polls), and the warp takes one decision
+      // forward: the stage's TMA (X and this CTA's codes) has landed, which
+      // also means the slot's previous MMAs are done (the producer issued it
+      // only after they were); dX: the slot is free
       bool free_slot = true;
-      if (kb >= S && lane == 0) free_slot = mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
+      if (!DX && lane == 0)
+        free_slot = mbar_wait(fullA0 + 8 * slot, (kb / S) & 1, ab);
+      else if (DX && kb >= S && lane == 0)
+        free_slot = mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
       if (!__shfl_sync(0xffffffffu, (int)free_slot, 0)) return false;
       unsigned char* bt = sm + TL::kSmB + slot * kBBytes;
       if (DX) {
@@ -574,13 +592,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       } else {
         // 8 chunks of 16 bytes (8 elements) a row; chunk c at (c ^ (row & 7))
         unsigned char* rowp = bt + (frow >> 3) * 1024 + (frow & 7) * 128;
+        uint32_t cw[CW];  // this thread's code words of the stage (TMA-landed)
+        {
+          const unsigned char* cs = sm + TL::kSmC + slot * TL::kCBytes + frow * 32 + fpart * (CW * 4);
+          if constexpr (CW == 4) {
+            const uint4 v = *reinterpret_cast<const uint4*>(cs);
+            cw[0] = v.x;
+            cw[1] = v.y;
+            cw[2] = v.z;
+            cw[3] = v.w;
+          } else {
+            const uint2 v = *reinterpret_cast<const uint2*>(cs);
+            cw[0] = v.x;
+            cw[1] = v.y;
+          }
+        }
 #pragma unroll
         for (int i = 0; i < CW; ++i) {
           const int c = fpart * CW + i;
           uint32_t qv[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 l = lut_at(r.c[i], j);
+            const float2 l = lut_at(cw[i], j);
             qv[j] = pack_rn<DT>(l.x * sv[0], l.y * sv[0]);
           }
           *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
@@ -591,18 +624,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       if (lane == 0) mbar_arrive(fullB0 + 8 * slot);
       return true;
     };
-    // a register ring of kPrefetch stages (static indices: fully unrolled)
-    Raw ring[kPrefetch];
+    if constexpr (DX) {
+      // a register ring of kPrefetch stages of codes and scales (static
+      // indices: fully unrolled)
+      Raw ring[kPrefetch];
 #pragma unroll
-    for (int i = 0; i < kPrefetch; ++i) fetch(i, ring[i]);
-    bool go = true;
-    for (int kb = 0; kb < nkb && go; kb += kPrefetch) {
+      for (int i = 0; i < kPrefetch; ++i) fetch(i, ring[i]);
+      bool go = true;
+      for (int kb = 0; kb < nkb && go; kb += kPrefetch) {
 #pragma unroll
-      for (int i = 0; i < kPrefetch; ++i) {
-        if (go && kb + i < nkb) {
-          go = convert(kb + i, ring[i]);
-          fetch(kb + i + kPrefetch, ring[i]);
+        for (int i = 0; i < kPrefetch; ++i) {
+          if (go && kb + i < nkb) {
+            const Raw& r = ring[i];
+            const float s0 = fmt == RQ_W_NF4 ? r.sraw[0] : sclut[r.c2b[0]] * r.sraw[0];
+            const float s1 = fmt == RQ_W_NF4 ? r.sraw[1] : sclut[r.c2b[1]] * r.sraw[1];
+            go = convert(kb + i, r, s0, s1);
+            fetch(kb + i + kPrefetch, ring[i]);
+          }
         }
+      }
+    } else {
+      // Forward: the codes come with the stage (TMA); the row's block scales
+      // are loaded 16 stages at a time, one group ahead of use (raw values in
+      // their own registers, so the loads stay in flight until the group is
+      // decoded).
+      struct Group {
+        uint32_t v[16];  // plain scales (fp32 bits) or c2 bytes
+        float s2[2];     // c2_scales of the group's first and last block
+      };
+      const int n = nh0 + frow;
+      auto group_fetch = [&](int gi, Group& q) {
+        const int s0 = gi * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) q.v[j] = 0u;
+        q.s2[0] = q.s2[1] = 0.0f;
+        if (s0 >= nkb || n >= N) return;
+        const int cnt = nkb - s0 < 16 ? nkb - s0 : 16;
+        const int64_t b0 = (int64_t)n * nbk + s0;
+        if (fmt == RQ_W_NF4) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < cnt) q.v[j] = __float_as_uint(load_scalar(g.w.scales, g.w.sdt, b0 + j));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < cnt) q.v[j] = ldg_pin_u8(g.w.c2 + b0 + j);
+          q.s2[0] = ldg_pin_f32(g.w.c2s + b0 / kDQBlock2);
+          q.s2[1] = ldg_pin_f32(g.w.c2s + (b0 + cnt - 1) / kDQBlock2);
+        }
+      };
+      Group gr;  // the next group's raw scales, in flight while 16 stages run
+      group_fetch(0, gr);
+      const Raw none{};
+      bool go = true;
+      for (int g0 = 0; g0 < nkb && go; g0 += 16) {
+        float sg[16];
+        const int64_t b0 = (int64_t)n * nbk + g0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          sg[j] = fmt == RQ_W_NF4 ? __uint_as_float(gr.v[j])
+                                  : sclut[gr.v[j] & 255u] *
+                                        (((b0 + j) / kDQBlock2) != (b0 / kDQBlock2) ? gr.s2[1] : gr.s2[0]);
+        group_fetch(g0 / 16 + 1, gr);
+#pragma unroll 1
+        for (int j = 0; j < 16 && go && g0 + j < nkb; ++j) go = convert(g0 + j, none, sg[j], 0.0f);
       }
     }
 
@@ -619,8 +704,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       T* y = static_cast<T*>(g.y);
       for (int cb = c_lo; cb < c_lo + BN / 2; cb += 32) {
         float acc[32], u[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + cb, acc);
-        if (has_lora) tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + BN + cb, u);
+        if (has_lora)
+          tmem_ld32x2(tmem + ((uint32_t)(quad * 32) << 16) + cb, tmem + ((uint32_t)(quad * 32) << 16) + BN + cb, acc, u);
+        else
+          tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + cb, acc);
         if (m >= M) continue;
         uint32_t pk[16];
 #pragma unroll
@@ -943,6 +1030,15 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
   } else {
     g.tmap = g.xmap;
     g.bmap = g.xmap;
+  }
+  if (!dx) {  // codes [N][K/2] bytes, a CTA's bn/2 rows x 32 bytes a stage
+    const uint64_t d[3] = {K / 2, N, 1}, sd[2] = {K / 2, 0};
+    const uint32_t b[3] = {32, (uint32_t)(bn / 2), 1};
+    const int rc = tensor_map_encode(CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_NONE, 2, a.w.q, d, sd, b,
+                                     &g.cmap);
+    if (rc != RQ_OK) return rc;
+  } else {
+    g.cmap = g.xmap;
   }
   g.w = a.w;
   g.bias = dx ? nullptr : a.bias;
