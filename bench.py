@@ -225,6 +225,24 @@ def run_ours(args, rank, world, device):
             graphs.append(gr)
         return graphs
 
+    if fused:
+        # probe the fused gather once, eagerly, before anything is captured:
+        # if any rank's calls gave up waiting for a peer (bounded wait in the
+        # kernel), every rank switches to the NCCL all-gather
+        step(0, True)
+        torch.cuda.synchronize(device)
+        t = torch.tensor([1 if any(pg.error() for pg in peers.values()) else 0], device=device, dtype=torch.int32)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if t.item():
+            print(f"rank {rank}: fused gather probe failed; using NCCL", file=sys.stderr, flush=True)
+            for pg in peers.values():
+                pg.close()
+            peers.clear()
+            fused = False
+            for si, (N, K) in enumerate(SHAPES):
+                for M in MS:
+                    gather_out[(si, M)] = torch.empty(world * M, N, dtype=torch.bfloat16, device=device)
+
     use_graphs = True
     graphs = capture(True)
 
