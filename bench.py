@@ -324,6 +324,7 @@ def run_ours(args, rank, world, device):
     cpu = cpu_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
     # configs[2] (prefill / training GEMM), single GPU
     prefill = prefill_leg(device) if (world == 1 and not args.no_prefill) else None
+    c5 = c5_leg(device) if (world == 1 and not args.no_prefill) else None
 
     if rank == 0:
         line = {
@@ -348,6 +349,7 @@ def run_ours(args, rank, world, device):
             "gpu_launches": args.steps * len(calls) * 2,
             "clocks": clocks,
             "prefill": prefill,
+            "c5": c5,
         }
         print(json.dumps(line), flush=True)
 
@@ -416,6 +418,66 @@ def prefill_leg(device, iters=5):
             "peak_kind": "measured sustained" if peak != 1400.0 else "fallback", "frac": round(tf / peak, 4),
             "config": "configs[2]: 7B shapes x M in {512,2048,8192}, forward and dX, NF4 double quant, r64 a128",
             "per_call_tflops": out}
+
+
+C5_SHAPES = [(8192, 28672), (28672, 8192)]
+
+
+def c5_leg(device, iters=3):
+    """SURVEY configs C5 on one GPU: the 70B-shaped projections W[N, K] in
+    {8192x28672, 28672x8192}, bf16 N(0, 0.015) weights as NF4 + double quant
+    and as INT8 with per-row scales, LoRA r=16 alpha=32; decode M=16 (HBM
+    GB/s of algorithmic bytes) and prefill M=4096 (TFLOP/s), forward calls
+    through the public layer op, CUDA-event timed (mean of `iters` calls
+    after 2 warm-up calls)."""
+    import torch.nn as nn
+    from rocm_qlora import LoRALinear, QuantLinear
+    from rocm_qlora.quantization import layer_ops, quantize_int8
+    out = {"nf4_dq": {}, "int8_row": {}}
+    for (N, K) in C5_SHAPES:
+        g = torch.Generator(device=device).manual_seed(N)
+        W = (torch.randn(N, K, generator=g, device=device) * 0.015).to(torch.bfloat16)
+        A = ((torch.rand(16, K, generator=g, device=device) * 2 - 1) / K ** 0.5).to(torch.bfloat16).contiguous()
+        B = (torch.randn(N, 16, generator=g, device=device) * 0.01).to(torch.bfloat16).contiguous()
+        for fmt in ("nf4_dq", "int8_row"):
+            if fmt == "nf4_dq":
+                lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=device)
+                with torch.no_grad():
+                    lin.weight.copy_(W)
+                ql = QuantLinear.from_linear(lin, bits=4)
+                ql.enable_double_quant()
+                wbytes = N * K // 2 + N * K // 64 + 4 * (N * K // 64 // 256 + 1)
+                del lin
+            else:
+                ql = QuantLinear(K, N, bits=8, bias=False).to(device)
+                q, s = quantize_int8(W, per_channel=True)
+                ql.weight_quant, ql.weight_scales = q, s
+                wbytes = N * K + 2 * N
+            w = ql.weight_view()
+            for M in (16, 4096):
+                x = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16)
+                fn = lambda: layer_ops.forward(w, x, None, A, B, 2.0)  # noqa: E731
+                for _ in range(2):
+                    fn()
+                torch.cuda.synchronize(device)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize(device)
+                us = e0.elapsed_time(e1) * 1e3 / iters
+                if M == 16:
+                    byts = wbytes + 2 * M * (K + N) + 2 * 16 * (K + N)
+                    out[fmt][f"{N}x{K}/M{M}"] = {"GB/s": round(byts / us / 1e3, 1), "us": round(us, 2)}
+                else:
+                    fl = 2.0 * M * N * K + 2.0 * M * 16 * (K + N)
+                    out[fmt][f"{N}x{K}/M{M}"] = {"TFLOP/s": round(fl / us / 1e6, 1), "us": round(us, 2)}
+                del x
+            del ql, w
+        del W
+    return {"config": "SURVEY C5 on one GPU: 70B shapes, NF4+DQ and INT8 per-row, LoRA r16 a32, forward",
+            "calls": out}
 
 
 def rotated_modules(layers, wsets):

@@ -90,12 +90,13 @@ constexpr int kLutReps = 16;                // copies of the code-byte table (on
 constexpr uint32_t kLutBytes = 256 * kLutReps * 8;
 constexpr uint32_t kSmemCap = 226 * 1024;   // dynamic shared memory budget (static + margin in the last KB)
 
-// Per-CTA shared-memory plan of a BN-wide pair tile (1 KB aligned offsets)
-template <int BN>
+// Per-CTA shared-memory plan of a BN-wide pair tile (1 KB aligned offsets);
+// I8: int8 weights (64 code bytes a row and stage instead of 32)
+template <int BN, bool I8>
 struct Tile {
   static constexpr int BNH = BN / 2;                  // weight rows (dX: output columns) a CTA
   static constexpr uint32_t kBBytes = BNH * BK * 2;   // 16 KB / 8 KB
-  static constexpr uint32_t kCBytes = BNH * 32;       // forward: this CTA's code bytes of one stage (4 / 2 KB)
+  static constexpr uint32_t kCBytes = BNH * (I8 ? 64 : 32);  // forward: this CTA's code bytes of one stage
   static constexpr uint32_t kStage = kABytes + kBBytes + kCBytes;
   static constexpr uint32_t kFixed = kABytes + kBBytes + kLutBytes + 1024 + 1024;  // LoRA tiles, LUT, sclut, align
   static constexpr int kFit = (int)((kSmemCap - kFixed) / kStage);
@@ -346,9 +347,9 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
   }
 }
 
-template <int DT, bool DX, int BN>
+template <int DT, bool DX, int BN, bool I8>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(const __grid_constant__ GemmArgs g) {
-  using TL = Tile<BN>;
+  using TL = Tile<BN, I8>;
   using T = typename DType<DT>::T;
   constexpr int S = TL::kStages, BNH = TL::BNH;
   constexpr uint32_t kBBytes = TL::kBBytes;
@@ -442,7 +443,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         if (rank == 0) mbar_expect_tx(fullB0 + 8 * slot, 16);  // the peer's "stage ready" signal
         mbar_expect_tx(fullA0 + 8 * slot, kABytes + (DX ? 0u : TL::kCBytes));
         tma_2d(sbase + TL::kSmA + slot * kABytes, &g.xmap, kb * BK, m0, fullA0 + 8 * slot);
-        if (!DX) tma_2d(sbase + TL::kSmC + slot * TL::kCBytes, &g.cmap, kb * 32, nh0, fullA0 + 8 * slot);
+        if (!DX) tma_2d(sbase + TL::kSmC + slot * TL::kCBytes, &g.cmap, kb * (I8 ? 64 : 32), nh0, fullA0 + 8 * slot);
         *reinterpret_cast<volatile int*>(&a_issued) = kb + 1;
       }
     }
@@ -498,17 +499,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
   } else {
     // ------------------------------------------------ dequant warps (2..9)
     // Forward: TPR threads share a tile row (weight row nh0 + dt / TPR of
-    // block kb), each converting CW 4-byte code words (8 elements, one
-    // 16-byte chunk each).  dX: warp (qb, part) = ((w-2) / 4, (w-2) % 4),
-    // lane p: weight rows 64 kb + 2p and +1, code bytes [8 part, 8 part + 8)
-    // of block nh0 / 64 + qb, i.e. 16 output columns; a warp's 32 lanes
-    // write one shared row's 32 distinct words.  Raw codes and scales are
+    // block kb), each converting CW 4-byte code words (NF4: 8 elements, one
+    // 16-byte chunk a word; int8: 4 elements, two words a chunk).  dX: warp
+    // (qb, part) = ((w-2) / 4, (w-2) % 4), lane p: weight rows 64 kb + 2p and
+    // +1, the 16 output columns [16 part, 16 part + 16) of block
+    // nh0 / 64 + qb (NF4: 8 code bytes a row, int8: 16); a warp's 32 lanes
+    // write one shared row's 32 distinct words.  dX codes and scales are
     // loaded kPrefetch stages ahead.
-    constexpr int TPR = 256 / BNH;  // forward: threads a row (2 or 4)
-    constexpr int CW = 8 / TPR;     // forward: code words a thread (4 or 2)
+    constexpr int CB = I8 ? 64 : 32;      // code bytes of a row and stage
+    constexpr int TPR = 256 / BNH;        // forward: threads a row (2 or 4)
+    constexpr int CW = (CB / 4) / TPR;    // forward: code words a thread
     constexpr int QB = BNH / 64;    // dX: quant blocks of a weight row a CTA covers (2 or 1)
     const int dt = tid - 64;
     const int fmt = g.w.fmt;
+    // first-level scales per block (NF4 / int8) or per row (int8 per-row);
+    // otherwise double-quantized (c2 code x c2_scales)
+    const bool plain = fmt == RQ_W_NF4 || fmt == RQ_W_INT8, rowsc = fmt == RQ_W_INT8_ROW;
     const int nbk = K / 64;
     const uint8_t* qb = static_cast<const uint8_t*>(g.w.q);
     const int frow = dt / TPR, fpart = dt % TPR;
@@ -523,13 +529,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       return v;
     };
     struct Raw {
-      uint32_t c[4];  // forward: CW code words of the row; dX: 2 words of each of the two rows
+      uint32_t c[8];  // dX: the code words of the two rows (NF4: 2 each, int8: 4 each)
       uint32_t c2b[2];
       float sraw[2];
     };
     auto fetch = [&](int kb, Raw& r) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) r.c[i] = 0u;
+      for (int i = 0; i < 8; ++i) r.c[i] = 0u;
       r.c2b[0] = r.c2b[1] = 0u;
       r.sraw[0] = r.sraw[1] = 0.0f;
       if (kb >= nkb) return;
@@ -538,15 +544,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         const int n = DX ? kb * 64 + 2 * p + h : nh0 + frow;
         const int blk = DX ? (nh0 >> 6) + dq : kb;
         if (DX ? (dx_active && blk < nbk) : n < N) {
-          const uint8_t* src = qb + (size_t)n * (K / 2) + (size_t)blk * 32;
-          if (DX) {  // forward codes arrive by TMA with the stage
+          const uint8_t* src = qb + (size_t)n * (size_t)(I8 ? K : K / 2) + (size_t)blk * CB;
+          if (DX && I8) {  // forward codes arrive by TMA with the stage
+            const uint4 v = ldg_pin4(reinterpret_cast<const uint4*>(src) + dpart);
+            r.c[4 * h] = v.x;
+            r.c[4 * h + 1] = v.y;
+            r.c[4 * h + 2] = v.z;
+            r.c[4 * h + 3] = v.w;
+          } else if (DX) {
             const uint2 v = ldg_pin2(reinterpret_cast<const uint2*>(src) + dpart);
             r.c[2 * h] = v.x;
             r.c[2 * h + 1] = v.y;
           }
           const int64_t bi = (int64_t)n * nbk + blk;
-          if (fmt == RQ_W_NF4) {
-            r.sraw[h] = load_scalar(g.w.scales, g.w.sdt, bi);
+          if (plain || rowsc) {
+            r.sraw[h] = load_scalar(g.w.scales, g.w.sdt, rowsc ? (int64_t)n : bi);
           } else {
             r.c2b[h] = ldg_pin_u8(g.w.c2 + bi);
             r.sraw[h] = ldg_pin_f32(g.w.c2s + bi / kDQBlock2);
@@ -572,7 +584,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         free_slot = mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
       if (!__shfl_sync(0xffffffffu, (int)free_slot, 0)) return false;
       unsigned char* bt = sm + TL::kSmB + slot * kBBytes;
-      if (DX) {
+      if (DX && I8) {
+        if (dx_active) {
+          // tile row kr (= output column), 16-bit pair (n, n+1) at word p;
+          // byte j of word i is output column 4 i + j of the thread's 16
+          const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float f0 = (float)(int8_t)(r.c[i] >> (8 * j)), f1 = (float)(int8_t)(r.c[4 + i] >> (8 * j));
+              const int kr = dq * 64 + dpart * 16 + i * 4 + j;
+              unsigned char* r0 = bt + (kr >> 3) * 1024 + (kr & 7) * 128 + colo;
+              *reinterpret_cast<uint32_t*>(r0 + ((colb ^ (kr & 7)) << 4)) = pack_rn<DT>(f0 * sv[0], f1 * sv[1]);
+            }
+        }
+      } else if (DX) {
         if (dx_active) {
           // tile row kr (= output column), 16-bit pair (n, n+1) at word p
           const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
@@ -594,8 +621,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         unsigned char* rowp = bt + (frow >> 3) * 1024 + (frow & 7) * 128;
         uint32_t cw[CW];  // this thread's code words of the stage (TMA-landed)
         {
-          const unsigned char* cs = sm + TL::kSmC + slot * TL::kCBytes + frow * 32 + fpart * (CW * 4);
-          if constexpr (CW == 4) {
+          const unsigned char* cs = sm + TL::kSmC + slot * TL::kCBytes + frow * CB + fpart * (CW * 4);
+          if constexpr (CW == 8) {
+            const uint4 v = *reinterpret_cast<const uint4*>(cs), v2 = *reinterpret_cast<const uint4*>(cs + 16);
+            cw[0] = v.x;
+            cw[1] = v.y;
+            cw[2] = v.z;
+            cw[3] = v.w;
+            cw[4] = v2.x;
+            cw[5] = v2.y;
+            cw[6] = v2.z;
+            cw[7] = v2.w;
+          } else if constexpr (CW == 4) {
             const uint4 v = *reinterpret_cast<const uint4*>(cs);
             cw[0] = v.x;
             cw[1] = v.y;
@@ -607,16 +644,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
             cw[1] = v.y;
           }
         }
+        if constexpr (I8) {
+          // int8: bf16/f16(float(q) * scale), two words a chunk
 #pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          const int c = fpart * CW + i;
-          uint32_t qv[4];
+          for (int i = 0; i < CW / 2; ++i) {
+            const int c = fpart * (CW / 2) + i;
+            uint32_t qv[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 l = lut_at(cw[i], j);
-            qv[j] = pack_rn<DT>(l.x * sv[0], l.y * sv[0]);
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t w = cw[2 * i + (j >> 1)];
+              const int b = (j & 1) * 16;
+              qv[j] = pack_rn<DT>((float)(int8_t)(w >> b) * sv[0], (float)(int8_t)(w >> (b + 8)) * sv[0]);
+            }
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
           }
-          *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < CW; ++i) {
+            const int c = fpart * CW + i;
+            uint32_t qv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 l = lut_at(cw[i], j);
+              qv[j] = pack_rn<DT>(l.x * sv[0], l.y * sv[0]);
+            }
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
+          }
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
@@ -636,8 +689,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         for (int i = 0; i < kPrefetch; ++i) {
           if (go && kb + i < nkb) {
             const Raw& r = ring[i];
-            const float s0 = fmt == RQ_W_NF4 ? r.sraw[0] : sclut[r.c2b[0]] * r.sraw[0];
-            const float s1 = fmt == RQ_W_NF4 ? r.sraw[1] : sclut[r.c2b[1]] * r.sraw[1];
+            const float s0 = (plain || rowsc) ? r.sraw[0] : sclut[r.c2b[0]] * r.sraw[0];
+            const float s1 = (plain || rowsc) ? r.sraw[1] : sclut[r.c2b[1]] * r.sraw[1];
             go = convert(kb + i, r, s0, s1);
             fetch(kb + i + kPrefetch, ring[i]);
           }
@@ -661,10 +714,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         if (s0 >= nkb || n >= N) return;
         const int cnt = nkb - s0 < 16 ? nkb - s0 : 16;
         const int64_t b0 = (int64_t)n * nbk + s0;
-        if (fmt == RQ_W_NF4) {
+        if (plain || rowsc) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (j < cnt) q.v[j] = __float_as_uint(load_scalar(g.w.scales, g.w.sdt, b0 + j));
+            if (j < cnt) q.v[j] = __float_as_uint(load_scalar(g.w.scales, g.w.sdt, rowsc ? (int64_t)n : b0 + j));
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -682,7 +735,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         const int64_t b0 = (int64_t)n * nbk + g0;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          sg[j] = fmt == RQ_W_NF4 ? __uint_as_float(gr.v[j])
+          sg[j] = (plain || rowsc) ? __uint_as_float(gr.v[j])
                                   : sclut[gr.v[j] & 255u] *
                                         (((b0 + j) / kDQBlock2) != (b0 / kDQBlock2) ? gr.s2[1] : gr.s2[0]);
         group_fetch(g0 / 16 + 1, gr);
@@ -952,7 +1005,12 @@ __global__ void __launch_bounds__(kLdThreads, 1) lora_down_tc_k(const __grid_con
 // ---------------------------------------------------------------- host side
 
 bool gemm_supported(const LinearArgs& a, bool dx) {
-  if (a.M < 64 || !is_nf4_fmt(a.w.fmt) || a.w.bs != 64 || a.w.K % 64) return false;
+  if (a.M < 64 || a.w.K % 64) return false;
+  if (is_nf4_fmt(a.w.fmt) || a.w.fmt == RQ_W_INT8) {
+    if (a.w.bs != 64) return false;  // one quant block a row and step
+  } else if (a.w.fmt != RQ_W_INT8_ROW) {
+    return false;
+  }
   if (dx && a.w.N % 64) return false;  // dX reduces over N in steps of 64 rows
   if (a.xdt != RQ_BF16 && a.xdt != RQ_F16) return false;
   if (a.r > 64 || (a.r > 0 && a.r % 8)) return false;
@@ -962,10 +1020,10 @@ bool gemm_supported(const LinearArgs& a, bool dx) {
   return a.w.N <= 0x7fffffff && a.w.K <= 0x7fffffff && a.M <= 0x7fffffff;
 }
 
-template <int DT, bool DX, int BN>
+template <int DT, bool DX, int BN, bool I8>
 static int gemm_run(const GemmArgs& g, uint64_t wout, uint64_t M, cudaStream_t st) {
-  constexpr uint32_t smem = Tile<BN>::kSmBytes;
-  const void* kern = (const void*)gemm_k<DT, DX, BN>;
+  constexpr uint32_t smem = Tile<BN, I8>::kSmBytes;
+  const void* kern = (const void*)gemm_k<DT, DX, BN, I8>;
   const int rc = ensure_smem_limit(kern, smem);
   if (rc != RQ_OK) return rc;
   // CTA pairs along x, output tiles along y, 256-row token pairs along z
@@ -983,12 +1041,24 @@ static int gemm_run(const GemmArgs& g, uint64_t wout, uint64_t M, cudaStream_t s
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_k<DT, DX, BN>, g);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_k<DT, DX, BN, I8>, g);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return RQ_ERR_CUDA;
   }
   return check_launch();
+}
+
+template <bool I8>
+static int gemm_pick(int xdt, bool dx, int bn, const GemmArgs& g, uint64_t wout, uint64_t M, cudaStream_t st) {
+  if (xdt == RQ_BF16) {
+    if (dx)
+      return bn == 256 ? gemm_run<RQ_BF16, true, 256, I8>(g, wout, M, st) : gemm_run<RQ_BF16, true, 128, I8>(g, wout, M, st);
+    return bn == 256 ? gemm_run<RQ_BF16, false, 256, I8>(g, wout, M, st)
+                     : gemm_run<RQ_BF16, false, 128, I8>(g, wout, M, st);
+  }
+  if (dx) return bn == 256 ? gemm_run<RQ_F16, true, 256, I8>(g, wout, M, st) : gemm_run<RQ_F16, true, 128, I8>(g, wout, M, st);
+  return bn == 256 ? gemm_run<RQ_F16, false, 256, I8>(g, wout, M, st) : gemm_run<RQ_F16, false, 128, I8>(g, wout, M, st);
 }
 
 // Tile width: 256 outputs a pair unless that leaves SMs idle, then 128.
@@ -1031,9 +1101,11 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
     g.tmap = g.xmap;
     g.bmap = g.xmap;
   }
-  if (!dx) {  // codes [N][K/2] bytes, a CTA's bn/2 rows x 32 bytes a stage
-    const uint64_t d[3] = {K / 2, N, 1}, sd[2] = {K / 2, 0};
-    const uint32_t b[3] = {32, (uint32_t)(bn / 2), 1};
+  const bool i8 = !is_nf4_fmt(a.w.fmt);
+  if (!dx) {  // codes [N][K/2] (int8: [N][K]) bytes, a CTA's bn/2 rows x 32 (64) bytes a stage
+    const uint64_t rowb = i8 ? K : K / 2;
+    const uint64_t d[3] = {rowb, N, 1}, sd[2] = {rowb, 0};
+    const uint32_t b[3] = {i8 ? 64u : 32u, (uint32_t)(bn / 2), 1};
     const int rc = tensor_map_encode(CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_NONE, 2, a.w.q, d, sd, b,
                                      &g.cmap);
     if (rc != RQ_OK) return rc;
@@ -1049,13 +1121,7 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
   g.K = (int)K;
   g.r = a.r > 0 ? a.r : 0;
   g.s = dx ? 1.0f : a.scaling;
-  if (a.xdt == RQ_BF16) {
-    if (dx)
-      return bn == 256 ? gemm_run<RQ_BF16, true, 256>(g, wout, M, st) : gemm_run<RQ_BF16, true, 128>(g, wout, M, st);
-    return bn == 256 ? gemm_run<RQ_BF16, false, 256>(g, wout, M, st) : gemm_run<RQ_BF16, false, 128>(g, wout, M, st);
-  }
-  if (dx) return bn == 256 ? gemm_run<RQ_F16, true, 256>(g, wout, M, st) : gemm_run<RQ_F16, true, 128>(g, wout, M, st);
-  return bn == 256 ? gemm_run<RQ_F16, false, 256>(g, wout, M, st) : gemm_run<RQ_F16, false, 128>(g, wout, M, st);
+  return i8 ? gemm_pick<true>(a.xdt, dx, bn, g, wout, M, st) : gemm_pick<false>(a.xdt, dx, bn, g, wout, M, st);
 }
 
 int gemm_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) { return gemm_launch(a, false, a.x, tdown, st); }

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import oracle as orc
-from tests.gpu_util import to_f32
+from tests.gpu_util import to_bits, to_f32
 from tests.inputs import layer_inputs
 from tests.test_gpu_linear import DTC, build_layer, oracle_wdeq
 from tests.tolerance import assert_matmul_close
@@ -125,3 +125,48 @@ def test_prefill_dx_non_power_of_two_scaling(M):
     wdeq = oracle_wdeq(lora.base_layer, N, K)
     dx_ref = orc.loralinear_dx(to_f32(inp.dY), wdeq, inp.A.numpy(), inp.B.numpy(), lora.scaling, DTC[torch.bfloat16])
     assert_matmul_close(to_f32(x.grad), dx_ref, DTC[torch.bfloat16], roundings=2)
+
+
+INT8_CASES = [
+    # fmt, N, K, M, r, dtype
+    ("int8", 520, 1024, 200, 16, torch.bfloat16),       # 128-wide pair tiles, ragged N and M
+    ("int8_row", 1000, 2048, 130, 8, torch.float16),    # per-output-row scales
+    ("int8", 4096, 1024, 1200, 16, torch.bfloat16),     # 256-wide pair tiles
+]
+
+
+@pytest.mark.parametrize("fmt,N,K,M,r,dt", INT8_CASES)
+def test_prefill_int8_gemm_vs_oracle(fmt, N, K, M, r, dt):
+    """INT8 weights (the reference's default bits=8, blockwise or per-row
+    scales) through the tcgen05 GEMM: forward Y and dX against the oracle."""
+    from rocm_qlora import LoRALinear, QuantLinear
+    from rocm_qlora import _native as nat
+    from rocm_qlora.quantization import quantize_int8
+    inp = layer_inputs(N, K, M, sigma=0.05, r=r, alpha=2 * r, w_dtype=dt, x_dtype=dt, seed=N + M, with_dy=True)
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(9)) * 0.1).to(dt)
+    if fmt == "int8_row":
+        ql = QuantLinear(K, N, bits=8, bias=True).cuda()
+        q, s = quantize_int8(inp.W.cuda(), per_channel=True)
+        ql.weight_quant, ql.weight_scales = q, s
+        ql.bias = bias.cuda()
+        lora = LoRALinear(ql, r=r, lora_alpha=2 * r).cuda().eval()
+        with torch.no_grad():
+            lora.lora_A.copy_(inp.A.cuda())
+            lora.lora_B.copy_(inp.B.cuda())
+        wdeq = orc.int8_dequantize(to_bits(q).reshape(-1), to_bits(s), DTC[dt], rows=N, cols=K).reshape(N, K)
+    else:
+        lora = build_layer(inp.W, 8, False, bias, r, 2 * r, inp.A, inp.B)
+        wdeq = oracle_wdeq(lora.base_layer, N, K)
+    x = inp.X.cuda().requires_grad_(True)
+    y = lora(x)
+    assert nat.lib().rq_last_path() == RQ_PATH_GEMM
+    y.backward(inp.dY.cuda())
+    torch.cuda.synchronize()
+    assert nat.lib().rq_last_path() == RQ_PATH_GEMM
+    assert ctypes_count(nat) == 0
+    xdt = DTC[dt]
+    A, B = inp.A.numpy(), inp.B.numpy()
+    y_ref = orc.loralinear_forward(to_f32(inp.X), wdeq, bias.float().numpy(), A, B, lora.scaling, xdt)
+    dx_ref = orc.loralinear_dx(to_f32(inp.dY), wdeq, A, B, lora.scaling, xdt)
+    assert_matmul_close(to_f32(y), y_ref, xdt, roundings=2)
+    assert_matmul_close(to_f32(x.grad), dx_ref, xdt, roundings=2)
