@@ -18,8 +18,11 @@
 //    K % 256 == 0 (each row's 256 contiguous bytes in one request pair, the
 //    DRAM-friendly shape), else as two 2-D 128-byte-wide boxes; both with
 //    128-byte swizzle;
-//  * 8 consumer warps: warp w multiplies block 8s + w of the stage for every
-//    tile; the warps meet in shared memory at the end in a fixed order
+//  * 16 consumer warps: warps w and w + 8 multiply block 8s + w of the
+//    stage, w for the pass's even tiles and w + 8 for the odd ones (two warps
+//    per block column: twice the warps in flight to cover the latency of the
+//    table lookups and MMA chains, half the accumulators each); the block
+//    columns meet in shared memory at the end in a fixed order
 //    (deterministic);
 //  * the multiply is mma.sync m16n8k16 with the weights as the A operand (16
 //    rows x 16 k) and X as B (8 tokens; two groups for M > 8), so M <= 8
@@ -55,7 +58,9 @@
 
 namespace rq {
 
-constexpr int kNfWarps = 8;  // consumer warps
+constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one per consumer warp pair)
+constexpr int kNfSplit = 2;                       // consumer warps per block column (they split the tiles)
+constexpr int kNfWarps = kStageBlocks * kNfSplit;  // consumer warps
 constexpr int kNfThreads = kNfWarps * 32;
 constexpr int kNfBlockThreads = kNfThreads + 32;  // + the producer warp
 constexpr uint32_t kWaitLimit = 1u << 22;         // polls of a barrier before a wait gives up
@@ -64,7 +69,6 @@ constexpr size_t kNfSmemMax = 227 * 1024 - 256;   // dynamic shared memory (stat
 constexpr int kNfMaxNT1 = 6;                      // 16-row tiles per pass, M <= 8
 constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 8
 constexpr int kNfMaxSlots = 8;                    // ring stages
-constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one per consumer warp)
 constexpr int kLoraDownCtas = 8;                  // CTAs of the small-M down-product kernel (lora_kernels.cu)
 
 // Bounded waits that ran out (a kernel that stopped early).
@@ -339,23 +343,28 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   T* tl = reinterpret_cast<T*>(smem + q.tl_off);
   T* stg = reinterpret_cast<T*>(smem + q.stg_off);
   const uint32_t lanesel = sbase + (uint32_t)(lane * 4);
-  // lane's code bytes in a slot: logical 16-byte chunk 2*(warp & 3) + (t >> 1)
-  // of 128-byte half warp >> 2 of tile row mma_row(g) (+16 nt + 8 h), half t & 1;
+  // warp pair bw = warp % 8 multiplies block bw of each stage; warp bw + 8 h
+  // takes the pass's tiles nt = h, h + 2, ...
+  const int bw = warp % kStageBlocks, th = warp / kStageBlocks;
+  // lane's code bytes in a slot: logical 16-byte chunk 2*(bw & 3) + (t >> 1)
+  // of 128-byte half bw >> 2 of tile row mma_row(g) (+16 nt + 8 h), half t & 1;
   // the 128-byte shared rows are swizzled by their index mod 8.
   //   3-D: shared row 2*r + half -> per tile 4096 bytes, per h 2048
   //   2-D: half at kBox, shared row r -> per tile 2048 bytes, per h 1024
   const int wide = q.wide;
-  const int pg = mma_row(g, wide), half = warp >> 2, lch = 2 * (warp & 3) + (t >> 1);
-  const uint32_t cofs = wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
-                             : (uint32_t)half * kBox + pg * 128 + (((lch ^ pg) << 4) | ((t & 1) << 3));
+  const int pg = mma_row(g, wide), half = bw >> 2, lch = 2 * (bw & 3) + (t >> 1);
+  // (a tile is 16 or 32 shared rows: the swizzle phase repeats per tile)
   const uint32_t tstep = wide ? 4096u : 2048u, hstep = tstep / 2;
+  const uint32_t cofs =
+      th * tstep + (wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
+                         : (uint32_t)half * kBox + pg * 128 + (((lch ^ pg) << 4) | ((t & 1) << 3)));
   // lane's X in a slot: token gr*8 + g (tokens past M read token M-1, results
-  // dropped), columns of block warp, 16 t .. 16 t + 15
+  // dropped), columns of block bw, 16 t .. 16 t + 15
   uint32_t xofs[MG];
 #pragma unroll
   for (int gr = 0; gr < MG; ++gr) {
     const int m = gr * 8 + g;
-    xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + warp * 128 + t * 32;
+    xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + bw * 128 + t * 32;
   }
 
   // decoded scales of the pass at rows [c0, c0+R) into sc in fragment order
@@ -405,7 +414,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       *reinterpret_cast<uint4*>(lut + v * 128 + (tid & 7) * 16) = make_uint4(w, w, w, w);
     }
   }
-  if (fmt != RQ_W_NF4)
+  if (fmt != RQ_W_NF4 && tid < 256)
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
 
   uint32_t u = 0;       // stages consumed (over all passes)
@@ -424,17 +433,19 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     consumer_sync();
     if (tid == 0) mbar_arrive(scempty);
 
-    float acc[NT][MG][4];
+    // this warp's tiles: nt = th + kNfSplit * i for i < NTW (nt < NT)
+    constexpr int NTW = (NT + kNfSplit - 1) / kNfSplit;
+    float acc[NTW][MG][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int i = 0; i < NTW; ++i)
 #pragma unroll
-      for (int gr = 0; gr < MG; ++gr) acc[nt][gr][0] = acc[nt][gr][1] = acc[nt][gr][2] = acc[nt][gr][3] = 0.0f;
-    const float* scw = sc + warp * sp + g * 2;
+      for (int gr = 0; gr < MG; ++gr) acc[i][gr][0] = acc[i][gr][1] = acc[i][gr][2] = acc[i][gr][3] = 0.0f;
+    const float* scw = sc + bw * sp + th * 16 + g * 2;
 
     for (int s = 0; s < nst; ++s, ++u) {
       const uint32_t slot = u % S;
       const bool ok = mbar_wait(full0 + 8 * slot, (u / S) & 1, abortp);
-      const int b = s * kStageBlocks + warp;
+      const int b = s * kStageBlocks + bw;
       if (ok && b < nbk) {
         const uint32_t sl = ring + slot * slot_bytes;
         uint32_t x[MG][8];
@@ -448,11 +459,13 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         }
         const float* sb = scw + (size_t)s * kStageBlocks * sp;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
+        for (int i = 0; i < NTW; ++i) {
+          const int nt = th + kNfSplit * i;
+          if (NT % kNfSplit != 0 && nt >= NT) break;
           uint2 lo, hi;
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + nt * tstep));
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + nt * tstep + hstep));
-          const float2 sv = *reinterpret_cast<const float2*>(sb + nt * 16);
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + i * kNfSplit * tstep));
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + i * kNfSplit * tstep + hstep));
+          const float2 sv = *reinterpret_cast<const float2*>(sb + i * kNfSplit * 16);
           float part[MG][4];
           kstep<DT, MG>(part, true, lut2<0>(lo.x, lanesel), lut2<0>(hi.x, lanesel), lut2<1>(lo.x, lanesel),
                         lut2<1>(hi.x, lanesel), x, 0);
@@ -464,10 +477,10 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
                         lut2<3>(hi.y, lanesel), x, 3);
 #pragma unroll
           for (int gr = 0; gr < MG; ++gr) {
-            acc[nt][gr][0] = fmaf(part[gr][0], sv.x, acc[nt][gr][0]);
-            acc[nt][gr][1] = fmaf(part[gr][1], sv.x, acc[nt][gr][1]);
-            acc[nt][gr][2] = fmaf(part[gr][2], sv.y, acc[nt][gr][2]);
-            acc[nt][gr][3] = fmaf(part[gr][3], sv.y, acc[nt][gr][3]);
+            acc[i][gr][0] = fmaf(part[gr][0], sv.x, acc[i][gr][0]);
+            acc[i][gr][1] = fmaf(part[gr][1], sv.x, acc[i][gr][1]);
+            acc[i][gr][2] = fmaf(part[gr][2], sv.y, acc[i][gr][2]);
+            acc[i][gr][3] = fmaf(part[gr][3], sv.y, acc[i][gr][3]);
           }
         }
       }
@@ -481,12 +494,17 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     if (stop) break;
     float* red = q.red_off ? reinterpret_cast<float*>(smem + q.red_off) : reinterpret_cast<float*>(smem + (ring - sbase));
     float4* red4 = reinterpret_cast<float4*>(red);
+    // partial sums [block column][tile][group][fragment]: the two warps of a
+    // column fill disjoint tiles
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int i = 0; i < NTW; ++i) {
+      const int nt = th + kNfSplit * i;
+      if (NT % kNfSplit != 0 && nt >= NT) break;
 #pragma unroll
       for (int gr = 0; gr < MG; ++gr)
-        red4[((warp * NT + nt) * MG + gr) * 32 + lane] =
-            make_float4(acc[nt][gr][0], acc[nt][gr][1], acc[nt][gr][2], acc[nt][gr][3]);
+        red4[((bw * NT + nt) * MG + gr) * 32 + lane] =
+            make_float4(acc[i][gr][0], acc[i][gr][1], acc[i][gr][2], acc[i][gr][3]);
+    }
     if (ch == 0) {
       asm volatile("griddepcontrol.wait;" ::: "memory");  // x.A^T of the kernel before
       if (p.r > 0) {
@@ -507,7 +525,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       if (nt >= ntl || rl >= R || m >= M) continue;
       float sum = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kNfWarps; ++w) sum += red[w * (NT * MG * 128) + e];
+      for (int w = 0; w < kStageBlocks; ++w) sum += red[w * (NT * MG * 128) + e];
       const int row = c0 + rl;
       float uu = 0.0f;
       if (has_lora) {
@@ -663,7 +681,7 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   off += align16((size_t)M * pl->nt * 16 * 2);
   pl->ring_off = (uint32_t)off;
   off += 1024;  // room to round the ring up to a 1 KB shared address
-  const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)kNfWarps * pl->nt * pl->mg * 512;
+  const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)kStageBlocks * pl->nt * pl->mg * 512;
   if (pl->chunks == 1) {
     pl->red_off = 0;
     pl->smem = off + (ring > red ? ring : red);
