@@ -230,6 +230,30 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 // barrier of the consumer warps only (the producer warp never joins it)
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNfThreads) : "memory"); }
 
+// the 16-bit element of `w` at bit 0 / bit 16, widened
+template <int DT>
+__device__ __forceinline__ float lo16_f32(uint32_t w) {
+  if constexpr (DT == RQ_BF16) return __uint_as_float(w << 16);
+  else return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+template <int DT>
+__device__ __forceinline__ float hi16_f32(uint32_t w) {
+  if constexpr (DT == RQ_BF16) return __uint_as_float(w & 0xffff0000u);
+  else return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+// acc + a[0]*b[0] + ... + a[7]*b[7] over eight packed 16-bit elements, one
+// fused multiply-add per element in element order
+template <int DT>
+__device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
+  const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc = fmaf(lo16_f32<DT>(av[i]), lo16_f32<DT>(bv[i]), acc);
+    acc = fmaf(hi16_f32<DT>(av[i]), hi16_f32<DT>(bv[i]), acc);
+  }
+  return acc;
+}
+
 template <int DT, int MG>
 __device__ __forceinline__ void kstep(float (&part)[MG][4], bool first, uint32_t a0, uint32_t a1, uint32_t a2,
                                       uint32_t a3, const uint32_t (&x)[MG][8], int j) {
@@ -370,7 +394,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   // decoded scales of the pass at rows [c0, c0+R) into sc in fragment order
   // [block][tile][MMA row g][g / g+8]
   const int fmt = p.w.fmt;
-  const float inv_nbk = 1.0f / (float)nbk;
   const unsigned char* raw = smem + q.raw_off;
   float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
   auto c2s_load = [&](int c0, int R) {  // the pass's c2_scales (one per 256 blocks)
@@ -382,10 +405,12 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   auto decode = [&](int c0, int R) {
     const int64_t f0 = (int64_t)c0 * nbk;
     const int total = R * nbk, inraw = (int)(raw_bytes(R) / esz);
+    // entry e = rl * nbk + b (row rl of the pass, block b), stepped by
+    // kNfThreads without a division per entry; its c2_scales entry is
+    // (f0 % 256 + e) / 256 of the pass's
+    const int f0lo = (int)(f0 & 255), dq = kNfThreads / nbk, dr = kNfThreads - dq * nbk;
+    int rl = tid / nbk, b = tid - rl * nbk;
     for (int e = tid; e < total; e += kNfThreads) {
-      int rl = __float2int_rz((float)e * inv_nbk), b = e - rl * nbk;
-      if (b < 0) --rl, b += nbk;
-      if (b >= nbk) ++rl, b -= nbk;
       float v;
       if (fmt == RQ_W_NF4) {
         v = e < inraw ? (esz == 4 ? reinterpret_cast<const float*>(raw)[e]
@@ -393,10 +418,13 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
                       : load_scalar(p.w.scales, p.w.sdt, f0 + e);
       } else {
         const uint32_t c = e < inraw ? raw[e] : __ldg(p.w.c2 + f0 + e);
-        v = sclut[c] * c2s_sm[((f0 + e) >> 8) - (f0 >> 8)];
+        v = sclut[c] * c2s_sm[(f0lo + e) >> 8];
       }
       const int rr = rl & 15, gg = mma_of_row(rr, q.wide);
       sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = v;
+      b += dr;
+      rl += dq;
+      if (b >= nbk) b -= nbk, ++rl;
     }
   };
 
@@ -418,6 +446,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
 
   uint32_t u = 0;       // stages consumed (over all passes)
+  uint32_t cslot = 0, cphase = 0;  // u % S and (u / S) & 1, kept without divisions
   uint32_t passes = 0;  // raw-scale copies waited for
   for (int ch = 0; ch < q.chunks; ++ch) {
     if (ch > 0) pass_tiles(ch, t0, t1);
@@ -443,8 +472,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     const float* scw = sc + bw * sp + th * 16 + g * 2;
 
     for (int s = 0; s < nst; ++s, ++u) {
-      const uint32_t slot = u % S;
-      const bool ok = mbar_wait(full0 + 8 * slot, (u / S) & 1, abortp);
+      const uint32_t slot = cslot;
+      const bool ok = mbar_wait(full0 + 8 * slot, cphase, abortp);
       const int b = s * kStageBlocks + bw;
       if (ok && b < nbk) {
         const uint32_t sl = ring + slot * slot_bytes;
@@ -486,6 +515,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * slot);  // this warp is done with the slot
+      if (++cslot == (uint32_t)S) cslot = 0, cphase ^= 1u;
     }
 
     consumer_sync();  // every warp is done with the ring (the partial sums may reuse it)
@@ -518,6 +548,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // MMA row g + 8 (e >> 1 & 1), token 8 gr + 2t + (e & 1)
     const bool has_bias = p.bias != nullptr, has_lora = p.r > 0;
     const T* lb = static_cast<const T*>(p.lora_b);
+    // rows of B and of x.A^T (shared, 16-byte aligned) in 16-byte pieces
+    const bool lora_vec = p.r % 8 == 0 && ((uintptr_t)lb % 16) == 0;
     T* y = static_cast<T*>(p.y);
     for (int e = tid; e < NT * MG * 128; e += kNfThreads) {
       const int nt = e / (MG * 128), gr = (e >> 7) % MG, ln = (e >> 2) & 31;
@@ -531,8 +563,14 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       if (has_lora) {
         const T* brow = lb + (size_t)row * p.r;
         const T* trow = tl + m * p.r;
+        if (lora_vec) {  // 16-byte loads, the same summation order
+          for (int j = 0; j < p.r; j += 8)
+            uu = dot8<DT>(*reinterpret_cast<const uint4*>(trow + j), __ldg(reinterpret_cast<const uint4*>(brow + j)),
+                          uu);
+        } else {
 #pragma unroll 8
-        for (int j = 0; j < p.r; ++j) uu = fmaf(DType<DT>::to_f32(trow[j]), DType<DT>::to_f32(__ldg(brow + j)), uu);
+          for (int j = 0; j < p.r; ++j) uu = fmaf(DType<DT>::to_f32(trow[j]), DType<DT>::to_f32(__ldg(brow + j)), uu);
+        }
       }
       const float bv = has_bias ? load_scalar(p.bias, p.bdt, row) : 0.0f;
       const T v = DType<DT>::from_f32(lora_epilogue<DT>(sum, has_bias, bv, uu, has_lora, p.s));

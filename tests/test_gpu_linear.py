@@ -116,6 +116,25 @@ def test_decode_gemv_nf4_dq_vs_oracle(N, K, M):
     assert_matmul_close(to_f32(x.grad), dx_ref, 1)
 
 
+@pytest.mark.parametrize("r", [8, 12, 3])
+@pytest.mark.parametrize("xdtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M", [1, 16])
+def test_decode_gemv_lora_ranks(r, xdtype, M):
+    """The decode GEMV's adapter epilogue for ranks that are a multiple of 8
+    (16-byte loads of B and x.A^T) and ranks that are not (element loads)."""
+    N, K = 600, 1024
+    inp = layer_inputs(N, K, M, sigma=0.05, r=r, alpha=2 * r, w_dtype=xdtype, x_dtype=xdtype, seed=100 + r + M,
+                       with_dy=True)
+    lora = build_layer(inp.W, 4, True, None, inp.r, inp.alpha, inp.A, inp.B)
+    x = inp.X.cuda().requires_grad_(True)
+    y = lora(x)
+    y.backward(inp.dY.cuda())
+    y_ref, dx_ref = _oracle_y_dx(lora, inp.X, inp.dY)
+    xdt = DTC[xdtype]
+    assert_matmul_close(to_f32(y), y_ref, xdt)
+    assert_matmul_close(to_f32(x.grad), dx_ref, xdt)
+
+
 @pytest.mark.parametrize("fmt", ["nf4", "int8", "int8_row"])
 @pytest.mark.parametrize("xdtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("M", [3, 16, 40])
