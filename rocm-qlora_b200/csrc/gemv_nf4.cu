@@ -229,6 +229,10 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 }
 // barrier of the consumer warps only (the producer warp never joins it)
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNfThreads) : "memory"); }
+// the producer warp's one-time signal that the CTA's mbarriers and flags are
+// initialized (it arrives, the consumers wait)
+__device__ __forceinline__ void start_arrive() { asm volatile("bar.arrive 2, %0;" ::"n"(kNfBlockThreads) : "memory"); }
+__device__ __forceinline__ void start_wait() { asm volatile("bar.sync 2, %0;" ::"n"(kNfBlockThreads) : "memory"); }
 
 // the 16-bit element of `w` at bit 0 / bit 16, widened
 template <int DT>
@@ -307,23 +311,32 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     t1 = t0 + NT < te ? t0 + NT : te;
   };
 
-  if (tid == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(full0 + 8 * i, 1);
-      mbar_init(empty0 + 8 * i, kNfWarps);
-    }
-    mbar_init(scfull, 1);
-    mbar_init(scempty, 1);
-    abort_flag = 0;
-    issued = 0;
-    raw_issued = 0;
-    producer_done = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-
   if (warp == kNfWarps) {
-    // ---- producer: stage u (over all passes) into slot u % S
+    // ---- producer: initializes the mbarriers and flags itself and starts
+    // issuing at once; the consumers wait for its start signal only before
+    // their first mbarrier wait (their table builds run meanwhile)
+    if (lane == 0) {
+      // every kernel parameter the issue path reads, loaded at once: the
+      // constant-bank misses overlap instead of following one another
+      asm volatile("" ::"r"(q.chunks), "r"(q.tpc), "r"(q.tiles), "r"(q.esz), "r"(q.raw_off), "r"(q.wide), "r"(S),
+                   "r"(ring), "r"(slot_bytes), "r"(M), "r"(N), "r"(nbk), "l"(rawsrc));
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&q.wmap) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&q.xmap) : "memory");
+      for (int i = 0; i < S; ++i) {
+        mbar_init(full0 + 8 * i, 1);
+        mbar_init(empty0 + 8 * i, kNfWarps);
+      }
+      mbar_init(scfull, 1);
+      mbar_init(scempty, 1);
+      abort_flag = 0;
+      issued = 0;
+      raw_issued = 0;
+      producer_done = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    start_arrive();
+    // ---- stage u (over all passes) into slot u % S
     if (lane == 0) {
       const uint32_t bytes = 2 * kBox + (uint32_t)M * 1024;
       uint32_t u = 0;
@@ -410,21 +423,33 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // (f0 % 256 + e) / 256 of the pass's
     const int f0lo = (int)(f0 & 255), dq = kNfThreads / nbk, dr = kNfThreads - dq * nbk;
     int rl = tid / nbk, b = tid - rl * nbk;
-    for (int e = tid; e < total; e += kNfThreads) {
-      float v;
-      if (fmt == RQ_W_NF4) {
-        v = e < inraw ? (esz == 4 ? reinterpret_cast<const float*>(raw)[e]
-                                  : load_scalar(raw, p.w.sdt, e))
-                      : load_scalar(p.w.scales, p.w.sdt, f0 + e);
-      } else {
-        const uint32_t c = e < inraw ? raw[e] : __ldg(p.w.c2 + f0 + e);
-        v = sclut[c] * c2s_sm[(f0lo + e) >> 8];
-      }
+    auto put = [&](float v) {
       const int rr = rl & 15, gg = mma_of_row(rr, q.wide);
       sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = v;
       b += dr;
       rl += dq;
       if (b >= nbk) b -= nbk, ++rl;
+    };
+    // the entries in the shared copy, then the tail (under 16 bytes) from
+    // global memory: separate loops, so that no shared entry waits on a
+    // global load the compiler would otherwise issue for every entry
+    int e = tid;
+    if (fmt == RQ_W_NF4) {
+      for (; e < inraw; e += kNfThreads)
+        put(esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e));
+      for (; e < total; e += kNfThreads) put(load_scalar(p.w.scales, p.w.sdt, f0 + e));
+    } else {
+      // four entries a thread per round, their loads ahead of the stores
+      // (four independent load chains instead of one)
+      for (; e + 3 * kNfThreads < inraw; e += 4 * kNfThreads) {
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = sclut[raw[e + i * kNfThreads]] * c2s_sm[(f0lo + e + i * kNfThreads) >> 8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) put(v[i]);
+      }
+      for (; e < inraw; e += kNfThreads) put(sclut[raw[e]] * c2s_sm[(f0lo + e) >> 8]);
+      for (; e < total; e += kNfThreads) put(sclut[__ldg(p.w.c2 + f0 + e)] * c2s_sm[(f0lo + e) >> 8]);
     }
   };
 
@@ -445,6 +470,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   if (fmt != RQ_W_NF4 && tid < 256)
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
 
+  start_wait();  // the producer's mbarriers and flags are initialized
   uint32_t u = 0;       // stages consumed (over all passes)
   uint32_t cslot = 0, cphase = 0;  // u % S and (u / S) & 1, kept without divisions
   uint32_t passes = 0;  // raw-scale copies waited for
