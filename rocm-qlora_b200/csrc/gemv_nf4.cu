@@ -139,6 +139,8 @@ struct Nf4Args {
   uint32_t aux_off;     //   256-entry second-level scale table,
   uint32_t tl_off;      //   staged x.A^T
   uint32_t stg_off;     //   a pass's outputs [M][NT*16] (gathering calls)
+  uint32_t bsm_off;     //   the pass's rows of LoRA B [NT*16][r]
+  int bsm;              // 1: B's rows are bulk-copied with the raw scales (one pass, r % 8 == 0)
 };
 
 // NF4 level c (the values of kNF4) from immediates: no memory access, so the
@@ -349,8 +351,15 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         if (ch > 0 && !mbar_wait(scempty, (ch - 1) & 1, abortp)) break;
         const int R = (t1 * 16 < N ? t1 * 16 : N) - t0 * 16;
         const uint32_t rb = raw_bytes(R);
-        mbar_expect_tx(scfull, rb);
+        // with one pass, the pass's rows of LoRA B too (a weight, written
+        // before the down-product kernel started; R * r * 2 bytes, a multiple
+        // of 16 at a 16-byte aligned source)
+        const uint32_t bb = q.bsm ? (uint32_t)(R * p.r * 2) : 0u;
+        mbar_expect_tx(scfull, rb + bb);
         if (rb) bulk_load(sbase + q.raw_off, rawsrc + (size_t)t0 * 16 * nbk * esz, rb, scfull);
+        if (bb)
+          bulk_load(sbase + q.bsm_off, static_cast<const unsigned char*>(p.lora_b) + (size_t)t0 * 16 * p.r * 2, bb,
+                    scfull);
         *raw_issuedp = ch + 1;
         for (int s = 0; s < nst; ++s, ++u) {
           const uint32_t slot = u % S;
@@ -589,7 +598,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       if (has_lora) {
         const T* brow = lb + (size_t)row * p.r;
         const T* trow = tl + m * p.r;
-        if (lora_vec) {  // 16-byte loads, the same summation order
+        if (q.bsm) {  // B's rows in shared memory (landed with the raw scales)
+          const T* bs = reinterpret_cast<const T*>(smem + q.bsm_off) + (size_t)rl * p.r;
+          for (int j = 0; j < p.r; j += 8)
+            uu = dot8<DT>(*reinterpret_cast<const uint4*>(trow + j), *reinterpret_cast<const uint4*>(bs + j), uu);
+        } else if (lora_vec) {  // 16-byte loads, the same summation order
           for (int j = 0; j < p.r; j += 8)
             uu = dot8<DT>(*reinterpret_cast<const uint4*>(trow + j), __ldg(reinterpret_cast<const uint4*>(brow + j)),
                           uu);
@@ -724,7 +737,7 @@ int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64
 struct Nf4Plan {
   int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
   size_t smem;
-  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off;
+  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
 };
 
 // [code table | scales | raw scales + c2_scales of a pass | second-level
@@ -743,6 +756,8 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   off += align16((size_t)M * (r > 0 ? r : 0) * 2);
   pl->stg_off = (uint32_t)off;
   off += align16((size_t)M * pl->nt * 16 * 2);
+  pl->bsm_off = (uint32_t)off;
+  off += align16((size_t)pl->nt * 16 * (r > 0 ? r : 0) * 2);
   pl->ring_off = (uint32_t)off;
   off += 1024;  // room to round the ring up to a 1 KB shared address
   const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)kStageBlocks * pl->nt * pl->mg * 512;
@@ -871,6 +886,8 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   q.aux_off = pl.aux_off;
   q.tl_off = pl.tl_off;
   q.stg_off = pl.stg_off;
+  q.bsm_off = pl.bsm_off;
+  q.bsm = pl.chunks == 1 && g.r > 0 && g.r % 8 == 0 && ((uintptr_t)g.lora_b % 16) == 0;
   if (g.xdt == RQ_BF16)
     return pl.mg == 2 ? nf4_nt<RQ_BF16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_BF16, 1>(q, pl.nt, pl.smem, pdl, st);
   return pl.mg == 2 ? nf4_nt<RQ_F16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_F16, 1>(q, pl.nt, pl.smem, pdl, st);
