@@ -42,7 +42,12 @@
 // just before this one.  This kernel is then launched as its programmatic
 // dependent: it streams the weights while the down product runs and waits
 // for it (griddepcontrol.wait) only before the epilogue reads x.A^T.  Every
-// other input was written before the down-product kernel started.
+// other input was written by kernels that had finished before the
+// down-product kernel let this one launch: the down product is itself a
+// programmatic dependent of the kernel before it and triggers this kernel
+// only after its own griddepcontrol.wait.  This kernel triggers at its
+// start, so the next layer's down product can be resident (waiting) while
+// it runs.
 //
 // All waits are bounded: a wait that runs out raises the CTA's abort flag,
 // the CTA lets its issued copies land (bounded) and returns without writing
@@ -286,6 +291,10 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots + 2];  // full[S], empty[S], scales full / empty
   __shared__ int abort_flag, issued, raw_issued, producer_done, stop;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  // The next layer's down-product kernel (a programmatic dependent) may be
+  // scheduled beside this grid now: it waits for this grid to finish before
+  // it reads anything or lets its own dependent start.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
   const int nbk = K >> 6;
   const int nst = (nbk + kStageBlocks - 1) / kStageBlocks;

@@ -176,7 +176,12 @@ __global__ void __cluster_dims__(kLoraCluster, 1, 1) __launch_bounds__(kLoraSmal
                       const typename DType<DT>::T* __restrict__ W2, int R, float pre_s, int do_pre,
                       typename DType<DT>::T* __restrict__ out) {
   using T = typename DType<DT>::T;
-  // the layer's GEMV may start now (it reads `out` only after this grid ends)
+  // Launched as the programmatic dependent of the kernel before it in the
+  // stream (it may be resident before that kernel ends): wait until that
+  // kernel has finished and its writes are visible (X may be its output),
+  // and only then let the layer's GEMV launch, which reads X at once and
+  // `out` only after this grid ends.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
   constexpr int RP = NT * 8;            // padded output columns
   constexpr int KB = NT <= 4 ? 8 : 4;   // k-steps per load batch
@@ -286,8 +291,22 @@ static int lora_small_launch(const void* X, int M, int Kr, const void* W2, int R
   auto kern = lora_down_small_k<DT, WT, NT>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
-  kern<<<kLoraCluster, kLoraSmallWarps * 32, smem, st>>>((const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre,
-                                                         (T*)out);
+  // programmatic dependent of the kernel before it (see the kernel's first lines)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kLoraCluster);
+  cfg.blockDim = dim3(kLoraSmallWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const T*)X, M, Kr, (const T*)W2, R, pre_s, do_pre, (T*)out);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return RQ_ERR_CUDA;
+  }
   return check_launch();
 }
 
