@@ -184,8 +184,10 @@ _ws: Dict[Tuple[int, int], torch.Tensor] = {}
 _ws_lock = threading.Lock()
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = (device.index, stream_ptr(device))
+def workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) -> torch.Tensor:
+    """The library workspace of (device, stream), at least nbytes; `stream`
+    is the stream's handle when the caller has it already."""
+    key = (device.index, stream_ptr(device) if stream is None else stream)
     with _ws_lock:
         buf = _ws.get(key)
         if buf is None or buf.numel() < nbytes:

@@ -45,8 +45,11 @@ class LoRALinear(nn.Module):
             if isinstance(self.lora_dropout, nn.Dropout) and self.training and self.lora_dropout.p > 0:
                 xd = self.lora_dropout(x)
             b = self.base_layer
-            return layer_ops.LoRAQuantFunction.apply(x, self.lora_A, self.lora_B, xd, b.weight_view(), b.bias,
-                                                     self.scaling)
+            if torch.is_grad_enabled() and (x.requires_grad or self.lora_A.requires_grad or
+                                            self.lora_B.requires_grad or (xd is not None and xd.requires_grad)):
+                return layer_ops.LoRAQuantFunction.apply(x, self.lora_A, self.lora_B, xd, b.weight_view(), b.bias,
+                                                         self.scaling)
+            return layer_ops.lora_forward(x, self.lora_A, self.lora_B, xd, b.weight_view(), b.bias, self.scaling)
         # any other base module: the reference's composition, unchanged
         if hasattr(self.base_layer, 'weight'):
             base_out = self.base_layer(x.to(self.base_layer.weight.dtype))

@@ -32,9 +32,13 @@ class WeightView:
         return self.q.device
 
     def args(self):
-        sc = self.scales
-        return (self.fmt, self.q.data_ptr(), nat.ptr(sc), nat.dtype_code(sc.dtype) if sc is not None else 0,
-                nat.ptr(self.c2), nat.ptr(self.c2_scales), self.N, self.K, self.block_size)
+        a = self.__dict__.get("_args")
+        if a is None:  # the view is immutable: its pointers never change
+            sc = self.scales
+            a = (self.fmt, self.q.data_ptr(), nat.ptr(sc), nat.dtype_code(sc.dtype) if sc is not None else 0,
+                 nat.ptr(self.c2), nat.ptr(self.c2_scales), self.N, self.K, self.block_size)
+            self.__dict__["_args"] = a
+        return a
 
 
 def weight_view(ql) -> WeightView:
@@ -70,6 +74,9 @@ def _check_device(w: WeightView, x: torch.Tensor) -> None:
         raise RuntimeError(f"QuantLinear buffers are on {w.q.device} but the input is on {x.device}")
 
 
+_ws_bytes = {}  # rq_linear_workspace_bytes by (M, N, K, r): a pure function of them
+
+
 def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: Optional[torch.Tensor],
             B: Optional[torch.Tensor], scaling: float, lora_x: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y[M, N] of LoRALinear.forward (eval) over QuantLinear.forward."""
@@ -80,14 +87,53 @@ def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: O
     dt = nat.dtype_code(x2d.dtype)
     r = 0 if A is None else A.shape[0]
     y = torch.empty(M, w.N, dtype=x2d.dtype, device=dev)
-    with torch.cuda.device(dev):
-        nbytes = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
-        ws = nat.workspace(dev, nbytes)
-        nat.check(L.rq_linear_forward(*w.args(), x2d.data_ptr(), dt, M, nat.ptr(lora_x), nat.ptr(bias),
-                                      nat.dtype_code(bias.dtype) if bias is not None else 0, nat.ptr(A), nat.ptr(B),
-                                      r, float(scaling), y.data_ptr(), ws.data_ptr(), ws.numel(),
-                                      nat.stream_ptr(dev)), "rq_linear_forward")
+    key = (M, w.N, w.K, r)
+    nbytes = _ws_bytes.get(key)
+    if nbytes is None:
+        nbytes = _ws_bytes[key] = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
+
+    def call():
+        st = nat.stream_ptr(dev)
+        ws = nat.workspace(dev, nbytes, st)
+        return L.rq_linear_forward(*w.args(), x2d.data_ptr(), dt, M, nat.ptr(lora_x), nat.ptr(bias),
+                                   nat.dtype_code(bias.dtype) if bias is not None else 0, nat.ptr(A), nat.ptr(B),
+                                   r, float(scaling), y.data_ptr(), ws.data_ptr(), ws.numel(), st)
+
+    # the library launches on the current stream of x's device, which must
+    # be the current device
+    if dev.index == torch.cuda.current_device():
+        rc = call()
+    else:
+        with torch.cuda.device(dev):
+            rc = call()
+    nat.check(rc, "rq_linear_forward")
     return y
+
+
+def _lora_operands(x, lora_A, lora_B, xd, bias):
+    """x and the adapter input as [M, K], A / B / bias in x's dtype."""
+    K = x.shape[-1]
+    dt = x.dtype
+    x2 = x.reshape(-1, K).contiguous()
+    xd2 = xd.reshape(-1, K).contiguous() if xd is not None else None
+    A = lora_A.to(dt).contiguous()
+    B = lora_B.to(dt).contiguous()
+    b = bias.to(dt).contiguous() if bias is not None else None
+    return x2, xd2, A, B, b
+
+
+def lora_forward(x, lora_A, lora_B, xd, w: WeightView, bias, scaling) -> torch.Tensor:
+    """LoRAQuantFunction's forward without autograd (nothing needs a
+    gradient): the same kernel call, none of the Function bookkeeping."""
+    x2, xd2, A, B, b = _lora_operands(x, lora_A, lora_B, xd, bias)
+    return forward(w, x2, b, A, B, scaling, lora_x=xd2).view(*x.shape[:-1], w.N)
+
+
+def quant_forward(x, w: WeightView, bias) -> torch.Tensor:
+    """QuantLinearFunction's forward without autograd."""
+    K = x.shape[-1]
+    b = bias.to(x.dtype).contiguous() if bias is not None else None
+    return forward(w, x.reshape(-1, K).contiguous(), b, None, None, 1.0).view(*x.shape[:-1], w.N)
 
 
 def forward_gather(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: Optional[torch.Tensor],
@@ -165,13 +211,7 @@ class LoRAQuantFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, lora_A, lora_B, xd, w: WeightView, bias, scaling):
-        K = x.shape[-1]
-        dt = x.dtype
-        x2 = x.reshape(-1, K).contiguous()
-        xd2 = xd.reshape(-1, K).contiguous() if xd is not None else None
-        A = lora_A.to(dt).contiguous()
-        B = lora_B.to(dt).contiguous()
-        b = bias.to(dt).contiguous() if bias is not None else None
+        x2, xd2, A, B, b = _lora_operands(x, lora_A, lora_B, xd, bias)
         y = forward(w, x2, b, A, B, scaling, lora_x=xd2)
         ctx.save_for_backward(x2 if xd2 is None else xd2, A, B)
         ctx.w, ctx.scaling, ctx.has_xd = w, scaling, xd is not None

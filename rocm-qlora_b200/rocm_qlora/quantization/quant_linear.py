@@ -103,14 +103,32 @@ class QuantLinear(nn.Module):
         return w.reshape(-1)[:n].reshape(self.original_shape)
 
     def weight_view(self) -> layer_ops.WeightView:
-        return layer_ops.weight_view(self)
+        """The C ABI's view of the quantized buffers, rebuilt only when a
+        buffer was replaced (module moves, new tensors) or written in place
+        (version counter), or the format flags changed."""
+        bufs = (self.weight_quant, getattr(self, "weight_scales", None), getattr(self, "c2", None),
+                getattr(self, "c2_scales", None))
+        if any(isinstance(t, torch.Tensor) and t.is_inference() for t in bufs):
+            # inference tensors carry no version counter: no cache
+            return layer_ops.weight_view(self)
+        key = (self.bits, self.block_size, getattr(self, "use_double_quant", False), getattr(self, "use_fp8_c2", True),
+               tuple((t.data_ptr(), t._version, t.shape, t.dtype) if isinstance(t, torch.Tensor) else None
+                     for t in bufs))
+        c = self.__dict__.get("_weight_view_cache")
+        if c is not None and c[0] == key:
+            return c[1]
+        wv = layer_ops.weight_view(self)
+        self.__dict__["_weight_view_cache"] = (key, wv)
+        return wv
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.merged_mode and self.merged_fp16_weight is not None:
             weight = self.merged_fp16_weight.to(x.dtype)
             bias = self.bias.to(x.dtype) if self.bias is not None else None
             return F.linear(x, weight, bias)
-        return layer_ops.QuantLinearFunction.apply(x, self.weight_view(), self.bias)
+        if torch.is_grad_enabled() and x.requires_grad:
+            return layer_ops.QuantLinearFunction.apply(x, self.weight_view(), self.bias)
+        return layer_ops.quant_forward(x, self.weight_view(), self.bias)
 
     def extra_repr(self) -> str:
         return f"in={self.in_features}, out={self.out_features}, bits={self.bits}, block_size={self.block_size}"

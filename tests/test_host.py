@@ -139,3 +139,28 @@ def test_workspace_size_query():
     assert L.rq_linear_workspace_bytes(16, 4096, 4096, 0) == 256
     assert L.rq_linear_workspace_bytes(16, 4096, 4096, 16) > 256
     assert L.rq_linear_workspace_bytes(-1, 1, 1, 1) == -1
+
+
+def test_weight_view_cache_follows_buffers():
+    """QuantLinear.weight_view() is reused while the quantized buffers are
+    unchanged and rebuilt after an in-place write, a replaced buffer or a
+    format change; inference tensors are never cached."""
+    import torch
+    from rocm_qlora import QuantLinear
+    ql = QuantLinear(256, 128, bits=4)
+    ql.weight_quant = torch.zeros(128 * 256 // 2, dtype=torch.uint8)
+    ql.weight_scales = torch.ones(128 * 256 // 64)
+    w1 = ql.weight_view()
+    assert ql.weight_view() is w1
+    assert w1.args() is w1.args()
+    ql.weight_quant.bitwise_or_(0)  # in place: the version counter moves
+    w2 = ql.weight_view()
+    assert w2 is not w1 and ql.weight_view() is w2
+    ql.weight_scales = ql.weight_scales.clone()  # a new tensor
+    w3 = ql.weight_view()
+    assert w3 is not w2 and w3.scales.data_ptr() == ql.weight_scales.data_ptr()
+    ql.block_size = 32
+    assert ql.weight_view() is not w3
+    with torch.inference_mode():
+        qi = QuantLinear(256, 128, bits=4)
+    assert qi.weight_view() is not qi.weight_view()
