@@ -32,6 +32,7 @@ template <> struct Mma16816<RQ_F16> {
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
+constexpr int kLoraDownCtas = 8;  // CTAs of the small-M down-product kernel (lora_kernels.cu)
 constexpr int kGemvMaxNT = 8;     // 8-row tiles held per warp at most (64 rows)
 
 struct GemvArgs {

@@ -55,10 +55,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
       lut[i] = pack2<DT>(kNF4[v & 15], kNF4[v >> 4]);
     }
   }
-  if (p.r > 0) {
-    const T* td = static_cast<const T*>(p.tdown);
-    for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
-  }
   const uint32_t* lane4 = lut + lane;
 
   const int tile_begin = (int)((int64_t)p.tiles * blockIdx.x / p.grid);
@@ -223,6 +219,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_k(const GemvArgs p) {
     for (int nt = 0; nt < NT; ++nt)
       if (nt < ntiles)
         red[(warp * NT + nt) * 32 + lane] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    if (ch == 0) {
+      // x.A^T comes from the down-product kernel launched just before; with
+      // an adapter this kernel is its programmatic dependent and waits for
+      // it only here, after streaming the first pass's weights (every other
+      // input was written by kernels that finished before the down product
+      // let this kernel launch)
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      if (p.r > 0) {
+        const T* td = static_cast<const T*>(p.tdown);
+        for (int i = tid; i < M * p.r; i += kGemvThreads) tl[i] = td[i];
+      }
+    }
     __syncthreads();
 
     const bool has_bias = p.bias != nullptr, has_lora = p.r > 0;
@@ -271,11 +279,14 @@ static size_t smem_for(int wk, int64_t K, int nt, int64_t M, int r) {
 }
 
 // Launch shape: two CTAs per SM, each owning ceil(N/8)/grid whole 8-row
-// tiles, processed in `chunks` passes of at most NT <= 8 tiles.
+// tiles, processed in `chunks` passes of at most NT <= 8 tiles.  With an
+// adapter the down-product kernel (one CTA on each of kLoraDownCtas SMs)
+// runs beside this one: those SMs hold one GEMV CTA, so the grid leaves
+// out one CTA for each (no CTA waits for a second wave).
 static void gemv_shape(int wk, int64_t N, int64_t K, int64_t M, int r, int* grid, int* tiles, int* chunks,
                        int* nt) {
   const int64_t T = (N + 7) / 8;
-  int64_t G = 2 * num_sms();
+  int64_t G = 2 * num_sms() - (r > 0 ? kLoraDownCtas : 0);
   if (G > T) G = T;
   const int64_t per = (T + G - 1) / G;
   int64_t ch = (per + kGemvMaxNT - 1) / kGemvMaxNT;
@@ -306,7 +317,22 @@ static int gemv_launch(const GemvArgs& g, size_t smem, cudaStream_t st) {
   auto kern = gemv_k<DT, WK, MT, NT>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
-  kern<<<g.grid, kGemvThreads, smem, st>>>(g);
+  // with an adapter: the programmatic dependent of the down-product kernel
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)g.grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = g.r > 0 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return RQ_ERR_CUDA;
+  }
   return check_launch();
 }
 

@@ -74,7 +74,6 @@ constexpr size_t kNfSmemMax = 227 * 1024 - 256;   // dynamic shared memory (stat
 constexpr int kNfMaxNT1 = 6;                      // 16-row tiles per pass, M <= 8
 constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 8
 constexpr int kNfMaxSlots = 8;                    // ring stages
-constexpr int kLoraDownCtas = 8;                  // CTAs of the small-M down-product kernel (lora_kernels.cu)
 
 // Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
