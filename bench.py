@@ -70,12 +70,15 @@ def peaks():
 
 # ----------------------------------------------------------- clock sampler
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling during the timed region.  The
+    raw samples go to bench_out/clocks_gpu<i>.csv (directory overridable
+    with RQ_BENCH_OUT); the JSON line carries their summary."""
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{index}.csv")
+        out = os.environ.get("RQ_BENCH_OUT", os.path.join(ROOT, "bench_out"))
+        self.path = os.path.join(out, f"clocks_gpu{index}.csv")
 
     def __enter__(self):
         os.makedirs(os.path.dirname(self.path), exist_ok=True)
@@ -424,7 +427,7 @@ C5_SHAPES = [(8192, 28672), (28672, 8192)]
 
 
 def c5_leg(device, iters=3):
-    """SURVEY configs C5 on one GPU: the 70B-shaped projections W[N, K] in
+    """The 70B-shaped projections on one GPU: W[N, K] in
     {8192x28672, 28672x8192}, bf16 N(0, 0.015) weights as NF4 + double quant
     and as INT8 with per-row scales, LoRA r=16 alpha=32; decode M=16 (HBM
     GB/s of algorithmic bytes) and prefill M=4096 (TFLOP/s), forward calls
@@ -476,7 +479,7 @@ def c5_leg(device, iters=3):
                 del x
             del ql, w
         del W
-    return {"config": "SURVEY C5 on one GPU: 70B shapes, NF4+DQ and INT8 per-row, LoRA r16 a32, forward",
+    return {"config": "70B-shaped projections on one GPU, NF4+DQ and INT8 per-row, LoRA r16 a32, forward",
             "calls": out}
 
 
