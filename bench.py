@@ -328,6 +328,7 @@ def run_ours(args, rank, world, device):
     # configs[2] (prefill / training GEMM), single GPU
     prefill = prefill_leg(device) if (world == 1 and not args.no_prefill) else None
     c5 = c5_leg(device) if (world == 1 and not args.no_prefill) else None
+    quant = quant_leg(device, no_cpu=args.no_cpu) if (world == 1 and not args.no_prefill) else None
 
     if rank == 0:
         line = {
@@ -353,6 +354,7 @@ def run_ours(args, rank, world, device):
             "clocks": clocks,
             "prefill": prefill,
             "c5": c5,
+            "quant": quant,
         }
         print(json.dumps(line), flush=True)
 
@@ -421,6 +423,96 @@ def prefill_leg(device, iters=5):
             "peak_kind": "measured sustained" if peak != 1400.0 else "fallback", "frac": round(tf / peak, 4),
             "config": "configs[2]: 7B shapes x M in {512,2048,8192}, forward and dX, NF4 double quant, r64 a128",
             "per_call_tflops": out}
+
+
+QUANT_SHAPES = [(4096, 4096), (8192, 28672)]
+
+
+def quant_leg(device, iters=5, cpu_seconds=4.0, no_cpu=False):
+    """North-star kernel (1): the quantize / dequantize streaming kernels on
+    bf16 weights [N, K] in {4096x4096, 8192x28672} (the second is 470 MB,
+    larger than L2), timed with CUDA events through the C ABI (mean of
+    `iters` calls after 2 warm-up calls).  Algorithmic bytes per call,
+    n = N*K, nb = n/64, ng = ceil(nb/256):
+      nf4_quantize      2n read + n/2 + 2nb written (codes, bf16 scales)
+      nf4_dequantize    n/2 + 2nb read + 4n written (fp32, the reference's output)
+      dq_quantize       4nb read (fp32 first-level scales) + nb + 4ng written
+      dq_dequantize     n/2 + nb + 4ng read + 4n written (fp32)
+      int8_quantize_rows 2n read + n + 2N written
+      int8_dequantize   n + 2N read + 4n written (fp32, per-row scales)
+    The reference's quantize_int4 (torch CPU ops, oracle/torch_port.py) is
+    timed beside it on a bounded sample of the 4096x4096 weight."""
+    from rocm_qlora import _native as nat
+    L = nat.lib()
+    hbm_peak, peak_kind = peaks()
+    st = torch.cuda.current_stream(device).cuda_stream
+    out = {}
+    for (N, K) in QUANT_SHAPES:
+        g = torch.Generator(device=device).manual_seed(N + K)
+        W = (torch.randn(N, K, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        n, nb = N * K, N * K // 64
+        ng = (nb + 255) // 256
+        packed = torch.empty(n // 2, dtype=torch.uint8, device=device)
+        sc = torch.empty(nb, dtype=torch.bfloat16, device=device)
+        c1 = torch.empty(nb, dtype=torch.float32, device=device)
+        c2 = torch.empty(ng * 256, dtype=torch.uint8, device=device)
+        c2s = torch.empty(ng, dtype=torch.float32, device=device)
+        fout = torch.empty(n, dtype=torch.float32, device=device)
+        q8 = torch.empty(n, dtype=torch.int8, device=device)
+        s8 = torch.empty(N, dtype=torch.bfloat16, device=device)
+        ops = {
+            "nf4_quantize": (lambda: L.rq_nf4_quantize(W.data_ptr(), nat.BF16, n, 64, packed.data_ptr(),
+                                                       sc.data_ptr(), st), 2 * n + n // 2 + 2 * nb),
+            "nf4_dequantize": (lambda: L.rq_nf4_dequantize(packed.data_ptr(), n // 2, sc.data_ptr(), nat.BF16, 64,
+                                                           fout.data_ptr(), nat.F32, st), n // 2 + 2 * nb + 4 * n),
+            "dq_quantize": (lambda: L.rq_dq_quantize_scales(c1.data_ptr(), nb, 256, 1, c2.data_ptr(), c2s.data_ptr(),
+                                                            st), 4 * nb + nb + 4 * ng),
+            "dq_dequantize": (lambda: L.rq_dq_dequantize(packed.data_ptr(), n, c2.data_ptr(), c2s.data_ptr(), 1, 64,
+                                                         256, fout.data_ptr(), nat.F32, st),
+                              n // 2 + nb + 4 * ng + 4 * n),
+            "int8_quantize_rows": (lambda: L.rq_int8_quantize_rows(W.data_ptr(), nat.BF16, N, K, q8.data_ptr(),
+                                                                   s8.data_ptr(), st), 2 * n + n + 2 * N),
+            "int8_dequantize": (lambda: L.rq_int8_dequantize(q8.data_ptr(), n, s8.data_ptr(), nat.BF16, 64, K,
+                                                             fout.data_ptr(), nat.F32, st), n + 2 * N + 4 * n),
+        }
+        res = {}
+        for name, (fn, byts) in ops.items():
+            if name == "dq_quantize":  # fp32 first-level scales of this weight
+                c1.copy_(sc.float())
+            for _ in range(2):
+                assert fn() == 0, name
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            us = e0.elapsed_time(e1) * 1e3 / iters
+            res[name] = {"GB/s": round(byts / us / 1e3, 1), "us": round(us, 2),
+                         "frac": round(byts / us / 1e3 / hbm_peak, 4)}
+        out[f"{N}x{K}"] = res
+        del W, packed, sc, c1, c2, c2s, fout, q8, s8
+    cpu = None
+    if not no_cpu:
+        from oracle import torch_port
+        torch.set_num_threads(os.cpu_count() or 1)
+        gc = torch.Generator().manual_seed(1)
+        Wc = (torch.randn(4096, 4096, generator=gc) * 0.02).to(torch.bfloat16)
+        rows, done, t_total = 256, 0, 0.0
+        while t_total < cpu_seconds or done == 0:
+            r0 = (done * rows) % 4096
+            t0 = time.perf_counter()
+            torch_port.nf4_quantize(Wc[r0:r0 + rows])
+            t_total += time.perf_counter() - t0
+            done += 1
+        n = done * rows * 4096
+        cpu = {"value": round((2 * n + n // 2 + 2 * n // 64) / t_total / 1e9, 4), "unit": "GB/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{done} quantize_int4 calls on 256-row slices of a 4096x4096 bf16 weight "
+                         f"({t_total:.1f} s)"}
+    return {"metric": "quantize / dequantize HBM GB/s of algorithmic bytes", "peak": hbm_peak,
+            "peak_kind": peak_kind, "calls": out, "cpu_quantize_int4": cpu}
 
 
 C5_SHAPES = [(8192, 28672), (28672, 8192)]

@@ -168,7 +168,8 @@ RQ_API int rq_linear_dx(int wfmt, const void* qweight, const void* scales, int s
  * device array inside the library, so nothing is allocated.  Calls whose
  * rq_linear_workspace_bytes(M, N, K, r) exceeds that size return
  * RQ_ERR_SCRATCH before touching the GPU.  The first call on a device looks
- * up the array's device address (make it before any stream capture).  All
+ * up the array's device address (make it before any stream capture); after
+ * cudaDeviceReset the next call looks it up again.  All
  * calls share the array: calls that may overlap on the GPU race and must not
  * be issued.  This entry point has no counterpart in the reference. */
 RQ_API int rq_linear_forward_noalloc(int wfmt, const void* qweight, const void* scales, int scale_dtype,

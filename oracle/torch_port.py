@@ -5,6 +5,9 @@ TEST / BASELINE INFRASTRUCTURE ONLY: bench.py's cpu_baseline leg and its
 implementation of the path.  It performs the same torch operations the
 reference performs on the CPU (its own code cannot travel to the GPU box):
 
+* NF4 quantize: per-block absmax, division in the input dtype, nearest
+  level by argmin over the fp32 distances, two codes per byte
+  (rocm_qlora/quantization/quant_ops.py:80-126);
 * NF4 dequantize: code table lookup in fp32, times the block scales
   (rocm_qlora/quantization/quant_ops.py:128-150);
 * double-quant first level: c2 (float8_e4m3fnuz) to fp32 times c2_scales
@@ -20,6 +23,21 @@ NF4_LEVELS = [
     -0.28444138169288635, -0.18477343022823334, -0.09105003625154495, 0.0,
     0.07958029955625534, 0.16093020141124725, 0.24611230194568634, 0.33791524171829224,
     0.44070982933044434, 0.5626170039176941, 0.7229568362236023, 1.0]
+
+
+def nf4_quantize(t: torch.Tensor, block_size: int = 64):
+    """quantize_int4 (quant_ops.py:80-126): (packed uint8, scales in t's dtype)."""
+    flat = t.reshape(-1)
+    pad = (-flat.numel()) % block_size
+    if pad:
+        flat = torch.cat([flat, flat.new_zeros(pad)])
+    blocks = flat.view(-1, block_size)
+    scales = blocks.abs().amax(dim=1, keepdim=True).clamp(min=1e-12)
+    n = blocks / scales
+    table = torch.tensor(NF4_LEVELS, dtype=torch.float32)
+    codes = (n.unsqueeze(-1) - table).abs().argmin(dim=-1).to(torch.uint8).reshape(-1)
+    packed = codes[0::2] | (codes[1::2] << 4)
+    return packed, scales.squeeze()
 
 
 def nf4_dequantize(packed: torch.Tensor, scales: torch.Tensor, block_size: int = 64) -> torch.Tensor:

@@ -13,8 +13,9 @@
 // library, kNoAllocScratchBytes each, until the process exits.  Host code
 // cannot use the array's name as a device address (it names a host-side
 // stand-in); its device address is looked up with cudaGetSymbolAddress the
-// first time the entry point runs on a device, with that device current.
-// That first call should therefore be made before any stream capture.
+// first time the entry point runs on a device, with that device current, and
+// again after the device's context was replaced (cudaDeviceReset).  That
+// first call should therefore be made before any stream capture.
 //
 // All calls on a device share the one array and it keeps whatever the last
 // call left there; the part that must start at zero (the arrival counters)
@@ -34,11 +35,40 @@ static_assert(kNoAllocScratchBytes % 256 == 0, "scratch must keep 256-byte align
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch on the current device (looked up once
-// per device).
+// Unique id of the calling thread's current CUDA context (cuCtxGetId, never
+// reused within a process), through the runtime's driver entry points so
+// the library does not link libcuda itself.  0 if the driver cannot say.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+static unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+  });
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || ctx == nullptr || get_id(ctx, &id) != 0) return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch for the current device and context.
+// The address is looked up with cudaGetSymbolAddress the first time a
+// device is used and again whenever the device's context has changed (after
+// cudaDeviceReset the module is loaded anew and the old address is gone).
 static int noalloc_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {};
+  static unsigned long long ctx_of[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -46,8 +76,11 @@ static int noalloc_scratch(void** out) {
     return RQ_ERR_CUDA;
   }
   if (dev < 0 || dev >= 64) return RQ_ERR_DEVICE;
+  // 0 before the thread has a context (the lookup below creates it) or when
+  // the driver cannot tell: then the address is looked up again
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  if (addr[dev] == nullptr || ctx == 0 || ctx != ctx_of[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -55,6 +88,7 @@ static int noalloc_scratch(void** out) {
       return RQ_ERR_CUDA;
     }
     addr[dev] = p;
+    ctx_of[dev] = current_context_id();
   }
   *out = addr[dev];
   return RQ_OK;

@@ -71,6 +71,7 @@ class LoRALinear(nn.Module):
         self.merged = True
         self.lora_A.data.zero_()
         self.lora_B.data.zero_()
+        layer_ops.forget_casts(self.lora_A, self.lora_B)
 
     def unmerge_lora(self) -> None:
         """Drop the merged fp16 weight and return to the quantized path."""
@@ -79,6 +80,7 @@ class LoRALinear(nn.Module):
         self.base_layer.merged_fp16_weight = None
         self.base_layer.merged_mode = False
         self.merged = False
+        layer_ops.forget_casts(self.lora_A, self.lora_B)
 
     def get_trainable_params(self) -> int:
         """Total number of trainable parameters in the LoRA layer."""

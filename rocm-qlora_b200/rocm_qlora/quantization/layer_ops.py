@@ -7,6 +7,7 @@ in the activation dtype with the same roundings as the reference's autograd
 of ``x @ A.T @ B.T * scaling`` (rocm_qlora/lora/lora_layer.py:67).
 """
 import ctypes
+import weakref
 from dataclasses import dataclass
 from typing import Optional
 
@@ -110,14 +111,48 @@ def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: O
     return y
 
 
+# Adapter parameters cast to the activation dtype, kept between calls: the
+# fp32 parameters would otherwise be cast (two kernels and two allocations)
+# on every layer call.  An entry is valid while the parameter keeps its
+# storage and in-place version (optimizer steps, copy_ and load_state_dict
+# bump the version); writes through ``.data`` do not, so code that writes
+# adapters that way calls forget_casts() (LoRALinear.merge_lora does).
+# Nothing is cached while a CUDA graph is being captured: a cast made there
+# only gets its values when the graph replays.
+_casts = {}  # id(parameter) -> (weakref to it, version, data_ptr, dtype, cast)
+
+
+def cast_param(p: torch.Tensor, dt: torch.dtype) -> torch.Tensor:
+    """`p` in dtype `dt`, contiguous, reusing the last cast while valid."""
+    if p.dtype == dt and p.is_contiguous():
+        return p
+    if p.is_cuda and torch.cuda.is_current_stream_capturing():
+        return p.detach().to(dt).contiguous()
+    key, ver, ptr = id(p), p._version, p.data_ptr()
+    e = _casts.get(key)
+    if e is not None and e[0]() is p and e[1] == ver and e[2] == ptr and e[3] == dt:
+        return e[4]
+    c = p.detach().to(dt).contiguous()
+    _casts[key] = (weakref.ref(p, lambda _r, k=key: _casts.pop(k, None)), ver, ptr, dt, c)
+    return c
+
+
+def forget_casts(*params: torch.Tensor) -> None:
+    """Drop the cached casts of `params` (after writes through ``.data``)."""
+    for p in params:
+        e = _casts.get(id(p))
+        if e is not None and e[0]() is p:
+            del _casts[id(p)]
+
+
 def _lora_operands(x, lora_A, lora_B, xd, bias):
     """x and the adapter input as [M, K], A / B / bias in x's dtype."""
     K = x.shape[-1]
     dt = x.dtype
     x2 = x.reshape(-1, K).contiguous()
     xd2 = xd.reshape(-1, K).contiguous() if xd is not None else None
-    A = lora_A.to(dt).contiguous()
-    B = lora_B.to(dt).contiguous()
+    A = cast_param(lora_A, dt)
+    B = cast_param(lora_B, dt)
     b = bias.to(dt).contiguous() if bias is not None else None
     return x2, xd2, A, B, b
 

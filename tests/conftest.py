@@ -15,3 +15,15 @@ for p in (ROOT, PKG):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device and the built sm_100a library")
+
+
+def pytest_terminal_summary(terminalreporter):
+    """One line per recorded parity check: the plain max-abs / RMS figure and
+    the count of outputs that passed only through the ulp allowance."""
+    from tests.tolerance import RECORDED
+    if not RECORDED:
+        return
+    tr = terminalreporter
+    tr.write_line("parity (max-abs/RMS, outputs over the bare 1e-2*RMS bar / outputs):")
+    for label, rel, n_ulp, n in RECORDED:
+        tr.write_line(f"  {label}: {rel:.2e}, {n_ulp}/{n}")

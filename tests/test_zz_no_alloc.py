@@ -69,7 +69,11 @@ def _forward(lib, lora, x, noalloc):
     return y.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("N,K,M,r", [(1024, 2048, 4, 16), (4096, 4096, 16, 16), (520, 1024, 40, 8)])
+# r = 96 with M <= 16 takes the split-K down product whose arrival counters
+# live in the scratch's first 256 bytes: the second call shows whether the
+# per-call clearing and the kernels' reset of the counters hold.
+@pytest.mark.parametrize("N,K,M,r", [(1024, 2048, 4, 16), (4096, 4096, 16, 16), (520, 1024, 40, 8),
+                                     (1024, 4096, 8, 96)])
 def test_noalloc_matches_forward_twice(lib, N, K, M, r):
     lora = _layer(N, K, r, seed=N + M)
     g = torch.Generator().manual_seed(M)
