@@ -213,7 +213,9 @@ RQ_API int rq_peer_close(void* ptr);
  * EVERY rank's copy of Y.  All pointers are device pointers valid on this
  * rank (peer allocations opened with rq_peer_open):
  *   outs[q]      rank q's Y (row stride ld elements of xdtype), q < world
- *   flags[q]     rank q's flag array, `world` uint32 (zero before first use)
+ *   flags[q]     rank q's flag array, 2 * world uint32 (zero before first
+ *                use): [0, world) the epoch each rank finished, [world,
+ *                2 * world) the epoch each rank entered
  *   my_flags     this rank's flag array (== flags[rank])
  *   ctrl         this rank's 4 uint32 of control state, zero before first
  *                use: [0] arrival counter (kernels leave it zero), [1] epoch
@@ -238,8 +240,11 @@ typedef struct RqGather {
  * the last CTA publishes this call's epoch to every rank's flags and waits,
  * bounded, for all of theirs).  Every rank must make the same sequence of
  * calls with the same M.  A rank's Y is rewritten by the next call that
- * names it, so the caller consumes each result before issuing a later call
- * on the same outputs.  Only the fused decode GEMV (NF4 formats, bf16/f16,
+ * names it, so each rank consumes each result (in stream order) before it
+ * issues its next call on the same outputs; a rank writes into the other
+ * ranks' Y only after every rank has entered the call (each rank announces
+ * its entry at the start of the kernel), so a faster rank never overwrites
+ * a result a slower rank is still reading.  Only the fused decode GEMV (NF4 formats, bf16/f16,
  * M <= 16) has this form: other arguments return RQ_ERR_UNSUPPORTED before
  * anything is launched, and the caller gathers with a collective instead.
  * Same-node NVLink peers only; one call in flight per RqGather. */

@@ -116,7 +116,7 @@ using namespace rq;
 
 extern "C" {
 
-int rq_abi_version(void) { return 1; }
+int rq_abi_version(void) { return 2; }
 
 const char* rq_status_string(int s) {
   switch (s) {

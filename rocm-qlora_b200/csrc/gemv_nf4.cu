@@ -123,6 +123,49 @@ __device__ void gather_arrive(const RqGather& g) {
   }
 }
 
+// Entry of a gathering call: its epoch (the value the call publishes at
+// its end) is the control block's epoch + 1; every CTA reads it at its
+// start, before any CTA can have arrived, so all CTAs read the same value.
+// CTA 0 announces to every rank that this rank has entered the call (its
+// stream has passed every earlier consumer of its Y).
+__device__ uint32_t gather_enter(const RqGather& g) {
+  const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(g.ctrl + 1) + 1;
+  if (blockIdx.x == 0)
+    for (int q = 0; q < g.world; ++q) {
+      uint32_t* f = g.flags[q] + g.world + g.rank;
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+    }
+  return e;
+}
+
+// Before a CTA stores its outputs into the other ranks' Y: wait (at most
+// about 2 s, one lane per rank) until every rank has entered this call, so
+// that no rank's copy of Y is overwritten while that rank may still be
+// reading the previous call's result.  Run by one full warp; returns false
+// (and raises the error flag) if a rank did not enter in time.
+__device__ bool gather_entered(const RqGather& g, uint32_t epoch, int lane) {
+  bool ok = true;
+  const uint64_t t0 = global_ns();
+  for (int q = lane; q < g.world; q += 32) {
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.my_flags + g.world + q) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (global_ns() - t0 > 2000000000ull) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && lane == 0) {
+    g.ctrl[2] = 1;
+    atomicAdd(&g_kernel_timeouts, 1u);
+  }
+  return ok;
+}
+
 struct Nf4Args {
   CUtensorMap wmap;  // codes: 3-D uint8 [N][K/256][128], box 128 x 2 x NT*16 (wide),
                      // else 2-D uint8 [N][K/2], box 128 x NT*16; 128-byte swizzle
@@ -288,7 +331,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   const GemvArgs& p = q.a;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots + 2];  // full[S], empty[S], scales full / empty
-  __shared__ int abort_flag, issued, raw_issued, producer_done, stop;
+  __shared__ int abort_flag, issued, raw_issued, producer_done, stop, gather_skip;
+  __shared__ uint32_t gather_epoch;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   // The next layer's down-product kernel (a programmatic dependent) may be
   // scheduled beside this grid now: it waits for this grid to finish before
@@ -486,6 +530,10 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   }
   if (fmt != RQ_W_NF4 && tid < 256)
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
+  if (p.gather && tid == 0) {
+    gather_epoch = gather_enter(p.gth);
+    gather_skip = 0;
+  }
 
   start_wait();  // the producer's mbarriers and flags are initialized
   uint32_t u = 0;       // stages consumed (over all passes)
@@ -584,6 +632,9 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         const T* td = static_cast<const T*>(p.tdown);
         for (int e = tid; e < M * p.r; e += kNfThreads) tl[e] = td[e];
       }
+      // every rank has entered this call before any of its Y is written
+      if (p.gather && warp == kNfWarps - 1 && !gather_entered(p.gth, gather_epoch, lane) && lane == 0)
+        gather_skip = 1;
     }
     consumer_sync();
 
@@ -629,22 +680,25 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     if (p.gather) {
       // the pass's outputs into every rank's Y[:, col + c0 ...]: 16-byte row
       // pieces where the destinations are 16-byte aligned (one NVLink write
-      // each), the rest element by element
+      // each), the rest element by element (nothing if a rank never entered
+      // the call: the output is then incomplete and the error flag is set)
       consumer_sync();
-      const int64_t ld = p.gth.ld, col0 = p.gth.col + c0;
-      const int R8 = ((ld | col0) & 7) == 0 ? (R & ~7) : 0, nb8 = R8 / 8;
-      for (int i = tid; i < M * nb8; i += kNfThreads) {
-        const int m = i / nb8, j = (i - m * nb8) * 8;
-        const uint4 v = *reinterpret_cast<const uint4*>(stg + m * (NT * 16) + j);
-        const size_t o = (size_t)m * ld + col0 + j;
-        for (int rq = 0; rq < p.gth.world; ++rq) *reinterpret_cast<uint4*>(static_cast<T*>(p.gth.outs[rq]) + o) = v;
-      }
-      const int rest = R - R8;
-      for (int i = tid; i < M * rest; i += kNfThreads) {
-        const int m = i / rest, j = R8 + (i - m * rest);
-        const T v = stg[m * (NT * 16) + j];
-        const size_t o = (size_t)m * ld + col0 + j;
-        for (int rq = 0; rq < p.gth.world; ++rq) static_cast<T*>(p.gth.outs[rq])[o] = v;
+      if (!gather_skip) {
+        const int64_t ld = p.gth.ld, col0 = p.gth.col + c0;
+        const int R8 = ((ld | col0) & 7) == 0 ? (R & ~7) : 0, nb8 = R8 / 8;
+        for (int i = tid; i < M * nb8; i += kNfThreads) {
+          const int m = i / nb8, j = (i - m * nb8) * 8;
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + m * (NT * 16) + j);
+          const size_t o = (size_t)m * ld + col0 + j;
+          for (int rq = 0; rq < p.gth.world; ++rq) *reinterpret_cast<uint4*>(static_cast<T*>(p.gth.outs[rq]) + o) = v;
+        }
+        const int rest = R - R8;
+        for (int i = tid; i < M * rest; i += kNfThreads) {
+          const int m = i / rest, j = R8 + (i - m * rest);
+          const T v = stg[m * (NT * 16) + j];
+          const size_t o = (size_t)m * ld + col0 + j;
+          for (int rq = 0; rq < p.gth.world; ++rq) static_cast<T*>(p.gth.outs[rq])[o] = v;
+        }
       }
     }
     consumer_sync();  // partial sums (and per-pass scales) are reused by the next pass

@@ -9,7 +9,10 @@ owns the memory that makes that possible:
 
   * Y [max_tokens, N] in the activation dtype, one per rank, mapped into
     every other rank's process (CUDA IPC, same node);
-  * a flag array of `world` uint32 per rank, also mapped everywhere;
+  * a flag array of 2 x `world` uint32 per rank, also mapped everywhere (the
+    epoch each rank finished, and the epoch each rank entered: a rank writes
+    into the others' Y only after all of them entered the call, so a result
+    that a slower rank is still reading is never overwritten);
   * 4 uint32 of control state per rank (arrival counter, epoch, error).
 
 Handles travel once through ``all_gather_object`` of the process group.
@@ -67,7 +70,7 @@ class PeerGather:
             handles, err = None, None
             try:
                 out = self._alloc(L, max_tokens * out_features * esz)
-                flags = self._alloc(L, 4 * self.world)
+                flags = self._alloc(L, 8 * self.world)  # finished and entered epochs per rank
                 self._ctrl = self._alloc(L, 16)
                 handles = (self._handle(L, out), self._handle(L, flags))
             except Exception as e:

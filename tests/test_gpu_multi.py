@@ -108,13 +108,137 @@ def _worker(rank: int, world: int, port: int, q) -> None:
             dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_gather_two_ranks():
+def _setup(rank, world, port):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "rocm-qlora_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    return dev
+
+
+def _sharded(dev, Nt, K, r, seed):
+    import torch.nn as nn
+    from rocm_qlora.distributed import ColumnParallelLinear
+    g = torch.Generator().manual_seed(seed)
+    W = (torch.randn(Nt, K, generator=g) * 0.02).to(torch.bfloat16)
+    A = (torch.rand(r, K, generator=g) * 2 - 1) / K ** 0.5
+    B = torch.randn(Nt, r, generator=g) * 0.01
+    lin = nn.Linear(K, Nt, bias=False, dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        lin.weight.copy_(W.to(dev))
+    cp = ColumnParallelLinear.from_linear(lin, bits=4, double_quant=True, lora_r=r, lora_alpha=2 * r,
+                                          gather_tokens=16)
+    with torch.no_grad():
+        cp.local.lora_A.copy_(A.to(dev))
+        cp.local.lora_B.copy_(B[cp.lo:cp.hi].to(dev))
+    return cp.eval()
+
+
+def _nccl(cp, x):
+    peer, cp.peer = cp.peer, None
+    try:
+        with torch.no_grad():
+            return cp(x).clone()
+    finally:
+        cp.peer = peer
+
+
+def _worker_slow_reader(rank: int, world: int, port: int, q) -> None:
+    """Back-to-back fused calls of one layer while rank 1 reads the first
+    result late (a 50 ms device sleep before its copy): rank 0's second call
+    must not overwrite rank 1's copy of the first result before rank 1 has
+    read it (rank 0 stores only after rank 1 entered the second call)."""
+    import torch.distributed as dist
+    ok = False
+    try:
+        dev = _setup(rank, world, port)
+        cp = _sharded(dev, 4096, 4096, 16, seed=11)
+        g = torch.Generator().manual_seed(12)
+        xa = torch.randn(4, 4096, generator=g).to(torch.bfloat16).to(dev)
+        xb = torch.randn(4, 4096, generator=g).to(torch.bfloat16).to(dev)
+        ya_ref, yb_ref = _nccl(cp, xa), _nccl(cp, xb)
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.no_grad():
+            ya = cp(xa)
+            if rank == 1:
+                torch.cuda._sleep(100_000_000)  # ~50 ms at 1.9 GHz before this rank reads its result
+            ya_read = ya.clone()
+            yb = cp(xb).clone()
+        torch.cuda.synchronize()
+        assert not cp.peer.error(), "a rank gave up waiting"
+        assert torch.equal(ya_read, ya_ref), f"rank {rank}: first result overwritten before it was read"
+        assert torch.equal(yb, yb_ref), f"rank {rank}: second result differs from NCCL"
+        cp.close()
+        ok = True
+        q.put((rank, "ok", ["slow reader ok"]))
+    except Exception as e:
+        q.put((rank, repr(e), []))
+    finally:
+        if dist.is_initialized():
+            if ok:
+                dist.barrier()
+            dist.destroy_process_group()
+
+
+def _worker_missing_rank(rank: int, world: int, port: int, q) -> None:
+    """Rank 1 skips one fused call (a host-side fault: the call is never
+    issued).  Rank 0's kernel gives up its bounded waits (about 2 s each),
+    returns with the error flag raised and counts the timeouts; nothing
+    hangs and both ranks close cleanly."""
+    import ctypes
+    import time
+    import torch.distributed as dist
+    from rocm_qlora import _native as nat
+    ok = False
+    try:
+        dev = _setup(rank, world, port)
+        cp = _sharded(dev, 2048, 1024, 16, seed=21)
+        x = torch.randn(2, 1024, generator=torch.Generator().manual_seed(22)).to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            cp(x)  # one good call on both ranks
+        torch.cuda.synchronize()
+        assert not cp.peer.error()
+        dist.barrier()
+        t0 = time.perf_counter()
+        if rank == 0:
+            with torch.no_grad():
+                cp(x)  # rank 1 never makes this call
+            torch.cuda.synchronize()
+            waited = time.perf_counter() - t0
+            c = ctypes.c_uint(0)
+            assert nat.lib().rq_take_kernel_timeouts(ctypes.byref(c)) == 0
+            assert cp.peer.error(), "the missing rank was not reported"
+            assert c.value >= 1, "no bounded wait counted a timeout"
+            assert waited < 30.0, f"the timed-out call took {waited:.1f} s"
+        dist.barrier()
+        cp.close()
+        ok = True
+        q.put((rank, "ok", ["missing rank reported"]))
+    except Exception as e:
+        q.put((rank, repr(e), []))
+    finally:
+        if dist.is_initialized():
+            if ok:
+                dist.barrier()
+            dist.destroy_process_group()
+
+
+def _run_two(target, n_msgs):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = []
@@ -124,4 +248,23 @@ def test_fused_gather_two_ranks():
         p.join(timeout=120)
     for rank, status, msgs in results:
         assert status == "ok", f"rank {rank}: {status}"
-        assert len(msgs) == len(CASES)
+        assert len(msgs) == n_msgs
+
+
+TWO_GPUS = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                              reason="needs two GPUs")
+
+
+@TWO_GPUS
+def test_fused_gather_two_ranks():
+    _run_two(_worker, len(CASES))
+
+
+@TWO_GPUS
+def test_fused_gather_slow_reader():
+    _run_two(_worker_slow_reader, 1)
+
+
+@TWO_GPUS
+def test_fused_gather_missing_rank_times_out():
+    _run_two(_worker_missing_rank, 1)
