@@ -60,7 +60,9 @@ extern "C" {
 /* ------------------------------------------------------------ utilities */
 RQ_API int rq_abi_version(void);                 /* bumps on any ABI change */
 RQ_API const char* rq_status_string(int status);
-RQ_API int rq_last_cuda_error(void);             /* cudaError_t of the last RQ_ERR_CUDA in this thread */
+/* cudaError_t of the last RQ_ERR_CUDA in this thread, or 10000 + the CUresult
+ * when a driver call (tensor-map encoding) failed */
+RQ_API int rq_last_cuda_error(void);
 /* Number of bounded in-kernel waits that ran out on the current device since
  * the last call (and reset it).  Nonzero means a kernel stopped early and its
  * output is not valid; it indicates a bug, never a normal condition.

@@ -11,7 +11,7 @@
 //    range), processed in `chunks` passes of NT tiles; every CTA but the last
 //    holds the same count, so one tensor-map box size serves all;
 //  * one producer thread streams the pass through a shared-memory ring of S
-//    stages with TMA: stage s holds 64-blocks [8s, 8s+8) of the pass's rows
+//    (up to 16) stages with TMA: stage s holds 64-blocks [8s, 8s+8) of the pass's rows
 //    and X's matching 512 columns (one box, M rows); stage completion and
 //    release go through mbarriers (transaction bytes / consumer-warp
 //    arrivals).  The codes come as one 3-D box [128 bytes][2][rows] when
@@ -34,20 +34,27 @@
 //    replicated 32 times (entry v, copy l at v*128 + l*4: lane l reads bank
 //    l), one byte permute, one multiply-add and one shared load;
 //  * block scales: the producer bulk-copies each pass's raw scale bytes
-//    (c2 codes, or the plain per-block scales) into shared memory first; the
-//    consumers decode them (fp8/int8 second level times c2_scales) into
-//    fragment order; the scale multiplies each block's fp32 partial.
+//    (c2 codes, or the plain per-block scales) into shared memory first; two
+//    decoder warps turn them, stage by stage, into the fp32 scales of the
+//    stage's blocks (fp8/int8 second level times c2_scales) in fragment
+//    order inside the stage's slot, one stage ahead of the consumers at
+//    most a ring ahead, so no pass waits for a whole decode before its first
+//    multiply and no per-pass scale table takes shared memory from the ring;
+//    the scale multiplies each block's fp32 partial.
 //
-// With LoRA the layer's down product x.A^T comes from the kernel launched
-// just before this one.  This kernel is then launched as its programmatic
-// dependent: it streams the weights while the down product runs and waits
-// for it (griddepcontrol.wait) only before the epilogue reads x.A^T.  Every
-// other input was written by kernels that had finished before the
-// down-product kernel let this one launch: the down product is itself a
-// programmatic dependent of the kernel before it and triggers this kernel
-// only after its own griddepcontrol.wait.  This kernel triggers at its
-// start, so the next layer's down product can be resident (waiting) while
-// it runs.
+// Every launch is programmatic (PDL).  With LoRA the layer's down product
+// x.A^T comes from the kernel launched just before this one; this kernel
+// then streams the weights while the down product runs and waits for it
+// (griddepcontrol.wait) only before the epilogue reads x.A^T ("early"
+// launch).  Every other input was written by kernels that had finished
+// before the down-product kernel let this one launch: the down product is
+// itself a programmatic dependent of the kernel before it and triggers this
+// kernel only after its own griddepcontrol.wait.  An early kernel triggers
+// its dependents at its start, so the next layer's down product can be
+// resident (waiting) while it runs.  Without LoRA the kernel reads nothing
+// (and announces nothing to the other ranks) before its own
+// griddepcontrol.wait, and releases its dependents only after it: its
+// prologue (barrier set-up, code table) overlaps the previous kernel's tail.
 //
 // All waits are bounded: a wait that runs out raises the CTA's abort flag,
 // the CTA lets its issued copies land (bounded) and returns without writing
@@ -67,13 +74,15 @@ constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one pe
 constexpr int kNfSplit = 2;                       // consumer warps per block column (they split the tiles)
 constexpr int kNfWarps = kStageBlocks * kNfSplit;  // consumer warps
 constexpr int kNfThreads = kNfWarps * 32;
-constexpr int kNfBlockThreads = kNfThreads + 32;  // + the producer warp
+constexpr int kNfDecWarps = 2;                    // warps decoding each stage's block scales
+constexpr int kNfDecThreads = kNfDecWarps * 32;
+constexpr int kNfBlockThreads = kNfThreads + kNfDecThreads + 32;  // consumers, decoders, producer
 constexpr uint32_t kWaitLimit = 1u << 22;         // polls of a barrier before a wait gives up
 constexpr uint32_t kLutBytes = 256 * 32 * 4;      // code table: 256 entries x 32 copies
-constexpr size_t kNfSmemMax = 227 * 1024 - 256;   // dynamic shared memory (static: the barriers)
+constexpr size_t kNfSmemMax = 227 * 1024 - 1024;  // dynamic shared memory (static: the barriers, < 1 KB)
 constexpr int kNfMaxNT1 = 6;                      // 16-row tiles per pass, M <= 8
 constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 8
-constexpr int kNfMaxSlots = 8;                    // ring stages
+constexpr int kNfMaxSlots = 16;                   // ring stages
 
 // Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
@@ -174,14 +183,16 @@ struct Nf4Args {
   int tiles;         // 16-row tiles of W
   int tpc;           // tiles per CTA (NT * chunks)
   int chunks;        // passes per CTA
-  int sp;            // floats per block row of the staged scales (NT * 16 + 2)
   int esz;           // bytes per raw scale (1: c2 codes; 2/4: plain scales)
   int wide;          // 1: 3-D code box (K % 256 == 0)
   int slots;         // ring stages S
-  uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X), a multiple of 1024
+  int early;         // 1: launched behind this library's down-product kernel, which waited for every kernel
+                     // before it: weights, scales and X are read from the start; 0: nothing is read (and
+                     // no dependent is released) before griddepcontrol.wait
+  uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X) + NT*512 (decoded scales), a multiple of 1024
+  uint32_t scl_off;     // offset of the decoded scales in a slot
   uint32_t ring_off;    // dynamic offsets: ring (rounded up to 1024 in the shared window),
   uint32_t red_off;     //   partial sums (0: the ring itself),
-  uint32_t sc_off;      //   decoded scales of a pass,
   uint32_t raw_off;     //   raw scale bytes of a pass, c2_scales of a pass,
   uint32_t aux_off;     //   256-entry second-level scale table,
   uint32_t tl_off;      //   staged x.A^T
@@ -282,6 +293,8 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 // initialized (it arrives, the consumers wait)
 __device__ __forceinline__ void start_arrive() { asm volatile("bar.arrive 2, %0;" ::"n"(kNfBlockThreads) : "memory"); }
 __device__ __forceinline__ void start_wait() { asm volatile("bar.sync 2, %0;" ::"n"(kNfBlockThreads) : "memory"); }
+// barrier of the two scale-decoder warps
+__device__ __forceinline__ void dec_sync() { asm volatile("bar.sync 3, %0;" ::"n"(kNfDecThreads) : "memory"); }
 
 // the 16-bit element of `w` at bit 0 / bit 16, widened
 template <int DT>
@@ -307,6 +320,17 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
   return acc;
 }
 
+// (a0, a1) += (p0, p1) * s as one packed fp32 FMA (each element rounded
+// once, as fmaf would)
+__device__ __forceinline__ void fma2(float& a0, float& a1, float p0, float p1, float s) {
+  unsigned long long a, pp, ss;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1,%2};" : "=l"(pp) : "f"(p0), "f"(p1));
+  asm("mov.b64 %0, {%1,%1};" : "=l"(ss) : "f"(s));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(pp), "l"(ss));
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+}
+
 template <int DT, int MG>
 __device__ __forceinline__ void kstep(float (&part)[MG][4], bool first, uint32_t a0, uint32_t a1, uint32_t a2,
                                       uint32_t a3, const uint32_t (&x)[MG][8], int j) {
@@ -330,24 +354,31 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   using T = typename DType<DT>::T;
   const GemvArgs& p = q.a;
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots + 2];  // full[S], empty[S], scales full / empty
+  // full[S] (TMA bytes), empty[S] (consumer warps), decoded[S] (one arrival
+  // per decoder warp), raw scales of a pass full / empty (the decoders
+  // release it)
+  __shared__ __align__(8) uint64_t bars[3 * kNfMaxSlots + 2];
   __shared__ int abort_flag, issued, raw_issued, producer_done, stop, gather_skip;
   __shared__ uint32_t gather_epoch;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  // The next layer's down-product kernel (a programmatic dependent) may be
-  // scheduled beside this grid now: it waits for this grid to finish before
-  // it reads anything or lets its own dependent start.
-  asm volatile("griddepcontrol.launch_dependents;");
+  // Behind the down-product kernel (early): the next layer's down product (a
+  // programmatic dependent, which waits for this grid to finish before it
+  // reads anything or lets its own dependent start) may be scheduled beside
+  // this grid now.  Otherwise the dependents are released only after this
+  // grid's own griddepcontrol.wait (below), so that a dependent that reads
+  // its weights before its wait only ever follows finished kernels.
+  if (q.early) asm volatile("griddepcontrol.launch_dependents;");
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
   const int nbk = K >> 6;
   const int nst = (nbk + kStageBlocks - 1) / kStageBlocks;
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
   const uint32_t ring = (sbase + q.ring_off + 1023u) & ~1023u;  // shared address (swizzle atoms are 1 KB)
-  const int sp = q.sp, S = q.slots;
+  const int S = q.slots;
   const uint32_t slot_bytes = q.slot_bytes;
   constexpr uint32_t kBox = NT * 16 * 128;  // one 128-byte-wide code box
   const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(bars), empty0 = full0 + kNfMaxSlots * 8;
-  const uint32_t scfull = full0 + 2 * kNfMaxSlots * 8, scempty = scfull + 8;
+  const uint32_t dec0 = full0 + 2 * kNfMaxSlots * 8;
+  const uint32_t scfull = full0 + 3 * kNfMaxSlots * 8, scempty = scfull + 8;
   // raw scale bytes of the pass at rows [c0, c0+R): one copy of the 16-byte
   // aligned part (the rest, under 16 bytes, is read directly)
   const int esz = q.esz;
@@ -365,9 +396,9 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     t1 = t0 + NT < te ? t0 + NT : te;
   };
 
-  if (warp == kNfWarps) {
+  if (warp == kNfWarps + kNfDecWarps) {
     // ---- producer: initializes the mbarriers and flags itself and starts
-    // issuing at once; the consumers wait for its start signal only before
+    // issuing at once; the other warps wait for its start signal only before
     // their first mbarrier wait (their table builds run meanwhile)
     if (lane == 0) {
       // every kernel parameter the issue path reads, loaded at once: the
@@ -379,6 +410,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       for (int i = 0; i < S; ++i) {
         mbar_init(full0 + 8 * i, 1);
         mbar_init(empty0 + 8 * i, kNfWarps);
+        mbar_init(dec0 + 8 * i, kNfDecWarps);
       }
       mbar_init(scfull, 1);
       mbar_init(scempty, 1);
@@ -390,16 +422,22 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     }
     __syncwarp();
     start_arrive();
+    if (!q.early) {
+      // every kernel before this one has finished (and its memory is
+      // visible) from here on; only now may this grid's dependents start
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      asm volatile("griddepcontrol.launch_dependents;");
+    }
     // ---- stage u (over all passes) into slot u % S
     if (lane == 0) {
       const uint32_t bytes = 2 * kBox + (uint32_t)M * 1024;
-      uint32_t u = 0;
+      uint32_t u = 0, slot = 0, round = 0;  // u % S and u / S
       for (int ch = 0; ch < q.chunks && !*abortp; ++ch) {
         int t0, t1;
         pass_tiles(ch, t0, t1);
         if (t1 <= t0) break;
-        // the pass's raw scales first (the buffer is free once the consumers
-        // decoded the previous pass's)
+        // the pass's raw scales first (the buffer is free once the decoders
+        // are done with the previous pass's)
         if (ch > 0 && !mbar_wait(scempty, (ch - 1) & 1, abortp)) break;
         const int R = (t1 * 16 < N ? t1 * 16 : N) - t0 * 16;
         const uint32_t rb = raw_bytes(R);
@@ -414,8 +452,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
                     scfull);
         *raw_issuedp = ch + 1;
         for (int s = 0; s < nst; ++s, ++u) {
-          const uint32_t slot = u % S;
-          if (u >= (uint32_t)S && !mbar_wait(empty0 + 8 * slot, ((u / S) - 1) & 1, abortp)) break;
+          if (round > 0 && !mbar_wait(empty0 + 8 * slot, (round - 1) & 1, abortp)) break;
           const uint32_t dst = ring + slot * slot_bytes, bar = full0 + 8 * slot;
           mbar_expect_tx(bar, bytes);
           if (q.wide) {
@@ -426,6 +463,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           }
           tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
           *issuedp = (int)(u + 1);
+          if (++slot == (uint32_t)S) slot = 0, ++round;
         }
       }
       __threadfence_block();
@@ -434,10 +472,97 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     return;
   }
 
+  const int fmt = p.w.fmt;
+  const unsigned char* raw = smem + q.raw_off;
+  float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
+  float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
+  const int wide = q.wide;
+
+  if (warp >= kNfWarps) {
+    // ---- scale decoders: per stage, the block scales of the pass's rows for
+    // the stage's 8 blocks (fp8 / int8 second level times c2_scales, or the
+    // plain per-block scales) into the slot, in fragment order
+    // [block][tile][MMA row g][rows g, g + 8]; then one arrival per warp on
+    // the slot's decoded barrier (the consumers wait for it and for the
+    // slot's TMA bytes).  Thread d takes block d % 8 of the stage and the pass
+    // rows d / 8 + 8 i.
+    const int d = tid - kNfThreads;
+    if (fmt != RQ_W_NF4)
+      for (int i = d; i < 256; i += kNfDecThreads)
+        sclut[i] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(i) : ieee_div((float)(int8_t)i, 127.0f);
+    start_wait();  // the producer's mbarriers and flags are initialized
+    const int bb = d & 7, r0 = d >> 3;
+    uint32_t u = 0, slot = 0, round = 0;
+    for (int ch = 0; ch < q.chunks; ++ch) {
+      int t0, t1;
+      pass_tiles(ch, t0, t1);
+      if (t1 <= t0) break;
+      const int c0 = t0 * 16;
+      const int R = (t1 * 16 < N ? t1 * 16 : N) - c0;
+      const int64_t f0 = (int64_t)c0 * nbk;
+      const int f0lo = (int)(f0 & 255), inraw = (int)(raw_bytes(R) / esz);
+      if (fmt != RQ_W_NF4) {  // the pass's c2_scales (one per 256 blocks)
+        dec_sync();           // the previous pass's are no longer read
+        const int n = (int)(((f0 + (int64_t)R * nbk - 1) >> 8) - (f0 >> 8)) + 1;
+        for (int i = d; i < n; i += kNfDecThreads) c2s_sm[i] = __ldg(p.w.c2s + (f0 >> 8) + i);
+        dec_sync();
+      }
+      // (the two decoder warps take the same barrier sequence whatever
+      // happens: a wait that gives up only skips work, every later wait then
+      // returns at once)
+      bool ok = mbar_wait(scfull, ch & 1, abortp);
+      for (int s = 0; s < nst; ++s, ++u) {
+        ok = ok && (round == 0 || mbar_wait(empty0 + 8 * slot, (round - 1) & 1, abortp));
+        if (!ok) {
+          if (++slot == (uint32_t)S) slot = 0, ++round;
+          continue;
+        }
+        float* dst = reinterpret_cast<float*>(smem + (ring - sbase) + slot * slot_bytes + q.scl_off);
+        const int b = s * kStageBlocks + bb;
+        if (b < nbk) {
+          // all of the thread's loads first, then the lookups and stores:
+          // 2 NT independent chains instead of one after the other
+          float v[2 * NT];
+          if (fmt == RQ_W_NF4) {
+#pragma unroll
+            for (int k = 0; k < 2 * NT; ++k) {
+              const int rl = r0 + 8 * k, e = rl * nbk + b;
+              v[k] = rl >= R ? 0.0f
+                     : e < inraw ? (esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e))
+                                 : load_scalar(p.w.scales, p.w.sdt, f0 + e);
+            }
+          } else {
+            uint32_t cb[2 * NT];
+#pragma unroll
+            for (int k = 0; k < 2 * NT; ++k) {
+              const int rl = r0 + 8 * k, e = rl * nbk + b;
+              cb[k] = rl >= R ? 0u : e < inraw ? (uint32_t)raw[e] : (uint32_t)__ldg(p.w.c2 + f0 + e);
+            }
+#pragma unroll
+            for (int k = 0; k < 2 * NT; ++k) {
+              const int rl = r0 + 8 * k, e = rl * nbk + b;
+              v[k] = rl >= R ? 0.0f : sclut[cb[k]] * c2s_sm[(f0lo + e) >> 8];
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 2 * NT; ++k) {
+            const int rl = r0 + 8 * k, rr = rl & 15;
+            dst[(bb * NT + (rl >> 4)) * 16 + mma_of_row(rr, wide) * 2 + (rr >> 3)] = v[k];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dec0 + 8 * slot);
+        if (++slot == (uint32_t)S) slot = 0, ++round;
+      }
+      // both decoder warps are done with this pass's raw scales
+      dec_sync();
+      if (d == 0) mbar_arrive(scempty);
+    }
+    return;
+  }
+
   // ---- consumers
   unsigned char* lut = smem;
-  float* sc = reinterpret_cast<float*>(smem + q.sc_off);
-  float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
   T* tl = reinterpret_cast<T*>(smem + q.tl_off);
   T* stg = reinterpret_cast<T*>(smem + q.stg_off);
   const uint32_t lanesel = sbase + (uint32_t)(lane * 4);
@@ -449,7 +574,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   // the 128-byte shared rows are swizzled by their index mod 8.
   //   3-D: shared row 2*r + half -> per tile 4096 bytes, per h 2048
   //   2-D: half at kBox, shared row r -> per tile 2048 bytes, per h 1024
-  const int wide = q.wide;
   const int pg = mma_row(g, wide), half = bw >> 2, lch = 2 * (bw & 3) + (t >> 1);
   // (a tile is 16 or 32 shared rows: the swizzle phase repeats per tile)
   const uint32_t tstep = wide ? 4096u : 2048u, hstep = tstep / 2;
@@ -464,61 +588,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     const int m = gr * 8 + g;
     xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + bw * 128 + t * 32;
   }
+  // lane's scales in a slot: block bw, tile th + 2 i, MMA row g (rows g, g + 8)
+  const uint32_t sofs = q.scl_off + (uint32_t)((bw * NT + th) * 16 + g * 2) * 4;
 
-  // decoded scales of the pass at rows [c0, c0+R) into sc in fragment order
-  // [block][tile][MMA row g][g / g+8]
-  const int fmt = p.w.fmt;
-  const unsigned char* raw = smem + q.raw_off;
-  float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
-  auto c2s_load = [&](int c0, int R) {  // the pass's c2_scales (one per 256 blocks)
-    if (fmt == RQ_W_NF4) return;
-    const int64_t f0 = (int64_t)c0 * nbk;
-    const int n = (int)(((f0 + (int64_t)R * nbk - 1) >> 8) - (f0 >> 8)) + 1;
-    for (int i = tid; i < n; i += kNfThreads) c2s_sm[i] = __ldg(p.w.c2s + (f0 >> 8) + i);
-  };
-  auto decode = [&](int c0, int R) {
-    const int64_t f0 = (int64_t)c0 * nbk;
-    const int total = R * nbk, inraw = (int)(raw_bytes(R) / esz);
-    // entry e = rl * nbk + b (row rl of the pass, block b), stepped by
-    // kNfThreads without a division per entry; its c2_scales entry is
-    // (f0 % 256 + e) / 256 of the pass's
-    const int f0lo = (int)(f0 & 255), dq = kNfThreads / nbk, dr = kNfThreads - dq * nbk;
-    int rl = tid / nbk, b = tid - rl * nbk;
-    auto put = [&](float v) {
-      const int rr = rl & 15, gg = mma_of_row(rr, q.wide);
-      sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = v;
-      b += dr;
-      rl += dq;
-      if (b >= nbk) b -= nbk, ++rl;
-    };
-    // the entries in the shared copy, then the tail (under 16 bytes) from
-    // global memory: separate loops, so that no shared entry waits on a
-    // global load the compiler would otherwise issue for every entry
-    int e = tid;
-    if (fmt == RQ_W_NF4) {
-      for (; e < inraw; e += kNfThreads)
-        put(esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e));
-      for (; e < total; e += kNfThreads) put(load_scalar(p.w.scales, p.w.sdt, f0 + e));
-    } else {
-      // four entries a thread per round, their loads ahead of the stores
-      // (four independent load chains instead of one)
-      for (; e + 3 * kNfThreads < inraw; e += 4 * kNfThreads) {
-        float v[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = sclut[raw[e + i * kNfThreads]] * c2s_sm[(f0lo + e + i * kNfThreads) >> 8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) put(v[i]);
-      }
-      for (; e < inraw; e += kNfThreads) put(sclut[raw[e]] * c2s_sm[(f0lo + e) >> 8]);
-      for (; e < total; e += kNfThreads) put(sclut[__ldg(p.w.c2 + f0 + e)] * c2s_sm[(f0lo + e) >> 8]);
-    }
-  };
-
-  int t0, t1;
-  pass_tiles(0, t0, t1);
-  if (t1 > t0) c2s_load(t0 * 16, (t1 * 16 < N ? t1 * 16 : N) - t0 * 16);
-  // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])) and
-  // the second-level table, built while the first stages are in flight
+  // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])),
+  // built while the first stages are in flight
   {
     const float lvl = nf4_level_imm(lane & 15);
 #pragma unroll 1
@@ -528,30 +602,23 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       *reinterpret_cast<uint4*>(lut + v * 128 + (tid & 7) * 16) = make_uint4(w, w, w, w);
     }
   }
-  if (fmt != RQ_W_NF4 && tid < 256)
-    sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
   if (p.gather && tid == 0) {
+    // the entry announcement follows every earlier kernel of this stream
+    if (!q.early) asm volatile("griddepcontrol.wait;" ::: "memory");
     gather_epoch = gather_enter(p.gth);
     gather_skip = 0;
   }
 
   start_wait();  // the producer's mbarriers and flags are initialized
+  consumer_sync();  // the code table is complete
   uint32_t u = 0;       // stages consumed (over all passes)
   uint32_t cslot = 0, cphase = 0;  // u % S and (u / S) & 1, kept without divisions
-  uint32_t passes = 0;  // raw-scale copies waited for
+  int t0, t1;
   for (int ch = 0; ch < q.chunks; ++ch) {
-    if (ch > 0) pass_tiles(ch, t0, t1);
+    pass_tiles(ch, t0, t1);
     if (t1 <= t0) break;
     const int ntl = t1 - t0, c0 = t0 * 16;
     const int R = (t1 * 16 < N ? t1 * 16 : N) - c0;
-    if (ch > 0) c2s_load(c0, R);
-    consumer_sync();  // tables and c2_scales in place
-    // the pass's raw scales have landed: decode them, then hand the buffer back
-    mbar_wait(scfull, ch & 1, abortp);
-    ++passes;
-    decode(c0, R);
-    consumer_sync();
-    if (tid == 0) mbar_arrive(scempty);
 
     // this warp's tiles: nt = th + kNfSplit * i for i < NTW (nt < NT)
     constexpr int NTW = (NT + kNfSplit - 1) / kNfSplit;
@@ -560,11 +627,10 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     for (int i = 0; i < NTW; ++i)
 #pragma unroll
       for (int gr = 0; gr < MG; ++gr) acc[i][gr][0] = acc[i][gr][1] = acc[i][gr][2] = acc[i][gr][3] = 0.0f;
-    const float* scw = sc + bw * sp + th * 16 + g * 2;
 
     for (int s = 0; s < nst; ++s, ++u) {
       const uint32_t slot = cslot;
-      const bool ok = mbar_wait(full0 + 8 * slot, cphase, abortp);
+      const bool ok = mbar_wait(full0 + 8 * slot, cphase, abortp) && mbar_wait(dec0 + 8 * slot, cphase, abortp);
       const int b = s * kStageBlocks + bw;
       if (ok && b < nbk) {
         const uint32_t sl = ring + slot * slot_bytes;
@@ -577,7 +643,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           x[gr][0] = u0.x, x[gr][1] = u0.y, x[gr][2] = u0.z, x[gr][3] = u0.w;
           x[gr][4] = u1.x, x[gr][5] = u1.y, x[gr][6] = u1.z, x[gr][7] = u1.w;
         }
-        const float* sb = scw + (size_t)s * kStageBlocks * sp;
 #pragma unroll
         for (int i = 0; i < NTW; ++i) {
           const int nt = th + kNfSplit * i;
@@ -585,7 +650,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           uint2 lo, hi;
           asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + i * kNfSplit * tstep));
           asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + i * kNfSplit * tstep + hstep));
-          const float2 sv = *reinterpret_cast<const float2*>(sb + i * kNfSplit * 16);
+          float2 sv;
+          asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(sv.x), "=f"(sv.y) : "r"(sl + sofs + i * kNfSplit * 64));
           float part[MG][4];
           kstep<DT, MG>(part, true, lut2<0>(lo.x, lanesel), lut2<0>(hi.x, lanesel), lut2<1>(lo.x, lanesel),
                         lut2<1>(hi.x, lanesel), x, 0);
@@ -597,10 +663,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
                         lut2<3>(hi.y, lanesel), x, 3);
 #pragma unroll
           for (int gr = 0; gr < MG; ++gr) {
-            acc[i][gr][0] = fmaf(part[gr][0], sv.x, acc[i][gr][0]);
-            acc[i][gr][1] = fmaf(part[gr][1], sv.x, acc[i][gr][1]);
-            acc[i][gr][2] = fmaf(part[gr][2], sv.y, acc[i][gr][2]);
-            acc[i][gr][3] = fmaf(part[gr][3], sv.y, acc[i][gr][3]);
+            fma2(acc[i][gr][0], acc[i][gr][1], part[gr][0], part[gr][1], sv.x);
+            fma2(acc[i][gr][2], acc[i][gr][3], part[gr][2], part[gr][3], sv.y);
           }
         }
       }
@@ -609,6 +673,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       if (++cslot == (uint32_t)S) cslot = 0, cphase ^= 1u;
     }
 
+    // with one pass, LoRA B's rows came with the pass's raw scales
+    if (ch == 0 && q.bsm) mbar_wait(scfull, 0, abortp);
     consumer_sync();  // every warp is done with the ring (the partial sums may reuse it)
     if (tid == 0) stop = *abortp;  // one decision for all consumers (the producer may set the flag any time)
     consumer_sync();
@@ -713,8 +779,9 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     for (uint32_t v = u; v < n; ++v)
       for (uint32_t i = 0; i < kWaitLimit && !mbar_test(full0 + 8 * (v % S), (v / S) & 1); ++i) {
       }
-    for (uint32_t v = passes; v < nr; ++v)
-      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, v & 1); ++i) {
+    // raw-scale copies complete in order: the last one issued covers all
+    if (nr > 0)
+      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, (nr - 1) & 1); ++i) {
       }
   }
   if (p.gather) {
@@ -778,10 +845,24 @@ static int tensor_map(const MapKey& k, CUtensorMap* out) {
   const cuuint64_t dims[3] = {k.d[0], k.d[1], k.d[2]}, strides[2] = {k.stride[0], k.stride[1]};
   const cuuint32_t box[3] = {k.box[0], k.box[1], k.box[2]}, es[3] = {1, 1, 1};
   CUtensorMap m;
-  const CUresult r = enc(&m, (CUtensorMapDataType)k.type, (cuuint32_t)k.rank, const_cast<void*>(k.ptr), dims, strides, box, es,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)k.swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return RQ_ERR_INVALID;
+  auto encode = [&] {
+    return enc(&m, (CUtensorMapDataType)k.type, (cuuint32_t)k.rank, const_cast<void*>(k.ptr), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)k.swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    // a thread that has only used the runtime API (autograd's backward
+    // thread, for one) may have no driver context bound yet: bind the
+    // current device's primary context, as every runtime call on it would,
+    // and encode again
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) r = encode();
+  }
+  if (r != CUDA_SUCCESS) {
+    set_cuda_error((cudaError_t)(kDriverErrorBase + (int)r));
+    return RQ_ERR_CUDA;
+  }
   std::lock_guard<std::mutex> lk(mu);
   if (cache.size() >= 4096) cache.clear();
   cache.emplace_back(k, m);
@@ -797,19 +878,19 @@ int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64
 }
 
 struct Nf4Plan {
-  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
+  int grid, tiles, tpc, chunks, nt, mg, esz, slots;
   size_t smem;
-  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
+  uint32_t slot_bytes, scl_off, ring_off, red_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
 };
 
-// [code table | scales | raw scales + c2_scales of a pass | second-level
-// table | x.A^T | staged outputs | ring (1 KB aligned) | partial sums];
-// with one pass the partial sums reuse the ring.
+// [code table | raw scales + c2_scales of a pass | second-level table |
+// x.A^T | staged outputs | LoRA B rows | ring (1 KB aligned) | partial
+// sums]; a slot is [codes | X | the stage's decoded scales]; with one pass
+// the partial sums reuse the ring.
 static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
-  pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
+  pl->scl_off = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
+  pl->slot_bytes = (pl->scl_off + (uint32_t)pl->nt * 512 + 1023u) & ~1023u;
   size_t off = kLutBytes;
-  pl->sc_off = (uint32_t)off;
-  off += align16((size_t)nbk * pl->sp * 4);
   pl->raw_off = (uint32_t)off;
   off += align16((size_t)pl->nt * 16 * nbk * pl->esz) + align16(((size_t)pl->nt * 16 * nbk / 256 + 2) * 4);
   pl->aux_off = (uint32_t)off;
@@ -851,9 +932,10 @@ static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool pdl, 
     pl->nt = (int)nt;
     pl->tpc = (int)(nt * ch);
     pl->grid = (int)((tiles + pl->tpc - 1) / pl->tpc);
-    // deepest ring that fits (at least 2 stages)
-    pl->sp = (int)(nt * 16 + 2);
-    for (int s = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots); s >= 2; --s) {
+    // deepest ring that fits (at least 2 stages; no more than the stages of
+    // all passes)
+    const int64_t all = nst * ch;
+    for (int s = (int)(all < kNfMaxSlots ? (all > 2 ? all : 2) : kNfMaxSlots); s >= 2; --s) {
       pl->slots = s;
       if (nf4_layout(pl, nbk, M, r) <= kNfSmemMax) return true;
     }
@@ -888,7 +970,8 @@ static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) 
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = 1;  // early or not, the kernel waits (griddepcontrol.wait) before reading what others wrote
+  (void)pdl;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q);
   if (e != cudaSuccess) {
     set_cuda_error(e);
@@ -937,13 +1020,13 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   q.tiles = pl.tiles;
   q.tpc = pl.tpc;
   q.chunks = pl.chunks;
-  q.sp = pl.sp;
   q.esz = pl.esz;
   q.slots = pl.slots;
   q.slot_bytes = pl.slot_bytes;
   q.ring_off = pl.ring_off;
   q.red_off = pl.red_off;
-  q.sc_off = pl.sc_off;
+  q.scl_off = pl.scl_off;
+  q.early = pdl ? 1 : 0;
   q.raw_off = pl.raw_off;
   q.aux_off = pl.aux_off;
   q.tl_off = pl.tl_off;

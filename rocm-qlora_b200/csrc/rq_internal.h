@@ -15,6 +15,10 @@ int last_path();
 // Records the CUDA error of the last failing launch in this thread.
 void set_cuda_error(cudaError_t e);
 
+// Driver-API failures (tensor-map encoding) are recorded as this base plus
+// the CUresult, so that they do not read as runtime error codes.
+constexpr int kDriverErrorBase = 10000;
+
 // Raises a kernel's dynamic shared memory limit to `bytes` on the current
 // device (once per kernel, device and size; thread-safe).
 int ensure_smem_limit(const void* kernel, size_t bytes);

@@ -10,11 +10,13 @@ the adapter term, so a one-ulp move of the base can become two when the
 adapter term is an exact half ulp (ties-to-even).  For bf16 one ulp exceeds
 1e-2 x RMS as soon as |y| >= 2 x RMS.  The check is therefore
 
-    |y - y_ref| <= 1e-2 * rms(y_ref) + roundings * ulp(y_ref)   (elementwise)
+    |y - y_ref| <= 1e-2 * rms(y_ref) + roundings * ulp   (elementwise)
 
 with `roundings` the number of output roundings after the accumulation in
 the reference's op sequence (1 for QuantLinear alone, 2 with the adapter),
-ulp = one unit in the last place of the stored dtype at y_ref (0 for fp32).
+ulp = one unit in the last place of the stored dtype at the larger of |y|
+and |y_ref| (0 for fp32): two values on either side of a power of two are
+one rounding apart at the upper binade's ulp.
 ``matmul_error`` reports the plain max-abs / RMS figure alongside.
 """
 import numpy as np
@@ -59,7 +61,10 @@ def assert_matmul_close(y, y_ref, dtype, roundings=2, label=None):
     assert np.all(np.isfinite(y)), "non-finite output"
     err, rms = matmul_error(y, y_ref)
     diff = np.abs(y - y_ref)
-    bound = RTOL_RMS * rms + roundings * ulp(y_ref, dtype)
+    # the rounding that produced an output erred by at most half an ulp of
+    # the output's own binade: next to a power of two the larger of the two
+    # values' ulps is the one that applies
+    bound = RTOL_RMS * rms + roundings * np.maximum(ulp(y_ref, dtype), ulp(y, dtype))
     bad = diff > bound
     if bad.any():
         i = np.argmax(diff - bound)
