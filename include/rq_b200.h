@@ -182,6 +182,19 @@ RQ_API int rq_linear_forward_noalloc(int wfmt, const void* qweight, const void* 
                       const void* lora_a, const void* lora_b, int r, float scaling,
                       void* y, void* stream);
 
+/* Numerics of the decode GEMV (M <= 16, NF4 formats).  0 (the default): the
+ * NF4 levels enter the tensor-core multiply rounded once to the activation
+ * dtype and the fp32 block scale multiplies each 64-wide partial sum.  The
+ * reference instead rounds level x scale to the activation dtype per weight;
+ * the two differ by a fixed error per code, within 1e-2 x RMS of the output
+ * for centred activations, but adding up over K when the activations share
+ * a sign (after a ReLU, say).  1 (exact): the kernel forms the reference's
+ * own weights, fp32 level x fp32 scale rounded to the activation dtype, per
+ * weight, so only the summation order differs; slower.  The environment
+ * variable RQ_DECODE_EXACT=1 selects 1 at the first call.  Applies to
+ * launches made after the call; no counterpart in the reference. */
+RQ_API void rq_set_decode_exact(int exact);
+
 /* Kernel family the last rq_linear_forward / rq_linear_dx of this thread
  * ran: RQ_PATH_GEMV (decode, M <= 16), RQ_PATH_GEMM (tcgen05 prefill GEMM),
  * RQ_PATH_GEMV_SLABS (the GEMV over 16-row slabs), RQ_PATH_SIMT (exact

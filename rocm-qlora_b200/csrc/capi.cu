@@ -135,6 +135,7 @@ const char* rq_status_string(int s) {
 int rq_last_cuda_error(void) { return g_last_cuda_error; }
 int rq_last_status(void) { return g_last_status; }
 int rq_last_path(void) { return rq::last_path(); }
+void rq_set_decode_exact(int exact) { rq::set_decode_exact(exact); }
 
 int rq_nf4_quantize(const void* x, int dtype, int64_t numel, int block_size, uint8_t* packed, void* scales,
                     void* stream) {

@@ -108,6 +108,9 @@ constexpr size_t kGemvSmemCap = 113 * 1024;  // two CTAs per SM
 // the launch (grid and tiling chosen inside; `pdl`: launched as the
 // programmatic dependent of the LoRA down-product kernel).
 bool gemv_nf4_fits(const QWeight& w, int64_t M, int r);
+// decode numerics (rq_set_decode_exact)
+bool decode_exact();
+void set_decode_exact(int on);
 int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st);
 
 }  // namespace rq

@@ -11,7 +11,7 @@
 //    range), processed in `chunks` passes of NT tiles; every CTA but the last
 //    holds the same count, so one tensor-map box size serves all;
 //  * one producer thread streams the pass through a shared-memory ring of S
-//    (up to 16) stages with TMA: stage s holds 64-blocks [8s, 8s+8) of the pass's rows
+//    stages with TMA: stage s holds 64-blocks [8s, 8s+8) of the pass's rows
 //    and X's matching 512 columns (one box, M rows); stage completion and
 //    release go through mbarriers (transaction bytes / consumer-warp
 //    arrivals).  The codes come as one 3-D box [128 bytes][2][rows] when
@@ -34,27 +34,20 @@
 //    replicated 32 times (entry v, copy l at v*128 + l*4: lane l reads bank
 //    l), one byte permute, one multiply-add and one shared load;
 //  * block scales: the producer bulk-copies each pass's raw scale bytes
-//    (c2 codes, or the plain per-block scales) into shared memory first; two
-//    decoder warps turn them, stage by stage, into the fp32 scales of the
-//    stage's blocks (fp8/int8 second level times c2_scales) in fragment
-//    order inside the stage's slot, one stage ahead of the consumers at
-//    most a ring ahead, so no pass waits for a whole decode before its first
-//    multiply and no per-pass scale table takes shared memory from the ring;
-//    the scale multiplies each block's fp32 partial.
+//    (c2 codes, or the plain per-block scales) into shared memory first; the
+//    consumers decode them (fp8/int8 second level times c2_scales) into
+//    fragment order; the scale multiplies each block's fp32 partial.
 //
-// Every launch is programmatic (PDL).  With LoRA the layer's down product
-// x.A^T comes from the kernel launched just before this one; this kernel
-// then streams the weights while the down product runs and waits for it
-// (griddepcontrol.wait) only before the epilogue reads x.A^T ("early"
-// launch).  Every other input was written by kernels that had finished
-// before the down-product kernel let this one launch: the down product is
-// itself a programmatic dependent of the kernel before it and triggers this
-// kernel only after its own griddepcontrol.wait.  An early kernel triggers
-// its dependents at its start, so the next layer's down product can be
-// resident (waiting) while it runs.  Without LoRA the kernel reads nothing
-// (and announces nothing to the other ranks) before its own
-// griddepcontrol.wait, and releases its dependents only after it: its
-// prologue (barrier set-up, code table) overlaps the previous kernel's tail.
+// With LoRA the layer's down product x.A^T comes from the kernel launched
+// just before this one.  This kernel is then launched as its programmatic
+// dependent: it streams the weights while the down product runs and waits
+// for it (griddepcontrol.wait) only before the epilogue reads x.A^T.  Every
+// other input was written by kernels that had finished before the
+// down-product kernel let this one launch: the down product is itself a
+// programmatic dependent of the kernel before it and triggers this kernel
+// only after its own griddepcontrol.wait.  This kernel triggers at its
+// start, so the next layer's down product can be resident (waiting) while
+// it runs.
 //
 // All waits are bounded: a wait that runs out raises the CTA's abort flag,
 // the CTA lets its issued copies land (bounded) and returns without writing
@@ -63,6 +56,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -74,15 +69,16 @@ constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one pe
 constexpr int kNfSplit = 2;                       // consumer warps per block column (they split the tiles)
 constexpr int kNfWarps = kStageBlocks * kNfSplit;  // consumer warps
 constexpr int kNfThreads = kNfWarps * 32;
-constexpr int kNfDecWarps = 2;                    // warps decoding each stage's block scales
-constexpr int kNfDecThreads = kNfDecWarps * 32;
-constexpr int kNfBlockThreads = kNfThreads + kNfDecThreads + 32;  // consumers, decoders, producer
+constexpr int kNfBlockThreads = kNfThreads + 32;  // + the producer warp
 constexpr uint32_t kWaitLimit = 1u << 22;         // polls of a barrier before a wait gives up
-constexpr uint32_t kLutBytes = 256 * 32 * 4;      // code table: 256 entries x 32 copies
-constexpr size_t kNfSmemMax = 227 * 1024 - 1024;  // dynamic shared memory (static: the barriers, < 1 KB)
+// Code table: 256 entries x 32 copies (one per lane) of the operand pair
+// (T[v & 15], T[v >> 4]), rounded to the activation dtype; in the exact
+// mode each copy is the pair of fp32 levels (8 bytes).
+__host__ __device__ constexpr uint32_t lut_bytes(bool exact) { return 256u * 32u * (exact ? 8u : 4u); }
+constexpr size_t kNfSmemMax = 227 * 1024 - 256;   // dynamic shared memory (static: the barriers)
 constexpr int kNfMaxNT1 = 6;                      // 16-row tiles per pass, M <= 8
 constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 8
-constexpr int kNfMaxSlots = 16;                   // ring stages
+constexpr int kNfMaxSlots = 8;                    // ring stages
 
 // Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
@@ -183,16 +179,14 @@ struct Nf4Args {
   int tiles;         // 16-row tiles of W
   int tpc;           // tiles per CTA (NT * chunks)
   int chunks;        // passes per CTA
+  int sp;            // floats per block row of the staged scales (NT * 16 + 2)
   int esz;           // bytes per raw scale (1: c2 codes; 2/4: plain scales)
   int wide;          // 1: 3-D code box (K % 256 == 0)
   int slots;         // ring stages S
-  int early;         // 1: launched behind this library's down-product kernel, which waited for every kernel
-                     // before it: weights, scales and X are read from the start; 0: nothing is read (and
-                     // no dependent is released) before griddepcontrol.wait
-  uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X) + NT*512 (decoded scales), a multiple of 1024
-  uint32_t scl_off;     // offset of the decoded scales in a slot
+  uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X), a multiple of 1024
   uint32_t ring_off;    // dynamic offsets: ring (rounded up to 1024 in the shared window),
   uint32_t red_off;     //   partial sums (0: the ring itself),
+  uint32_t sc_off;      //   decoded scales of a pass,
   uint32_t raw_off;     //   raw scale bytes of a pass, c2_scales of a pass,
   uint32_t aux_off;     //   256-entry second-level scale table,
   uint32_t tl_off;      //   staged x.A^T
@@ -234,6 +228,16 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
 template <int KB>
 __device__ __forceinline__ uint32_t lut2(uint32_t word, uint32_t lanesel) {
   return lds_u32(__byte_perm(word, 0u, 0x4440u | KB) * 128u + lanesel);
+}
+// fp32 level pair (T[lo nibble], T[hi nibble]) of code byte KB of `word` for
+// this lane (lanesel: shared address of the table plus lane*8)
+template <int KB>
+__device__ __forceinline__ uint2 lut4(uint32_t word, uint32_t lanesel) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "r"(__byte_perm(word, 0u, 0x4440u | KB) * 256u + lanesel));
+  return v;
 }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -293,8 +297,6 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 // initialized (it arrives, the consumers wait)
 __device__ __forceinline__ void start_arrive() { asm volatile("bar.arrive 2, %0;" ::"n"(kNfBlockThreads) : "memory"); }
 __device__ __forceinline__ void start_wait() { asm volatile("bar.sync 2, %0;" ::"n"(kNfBlockThreads) : "memory"); }
-// barrier of the two scale-decoder warps
-__device__ __forceinline__ void dec_sync() { asm volatile("bar.sync 3, %0;" ::"n"(kNfDecThreads) : "memory"); }
 
 // the 16-bit element of `w` at bit 0 / bit 16, widened
 template <int DT>
@@ -331,6 +333,25 @@ __device__ __forceinline__ void fma2(float& a0, float& a1, float p0, float p1, f
   asm("mov.b64 {%0,%1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
 }
 
+// The reference's dequantized weight pair, rounded as it rounds it: each
+// fp32 level times the fp32 block scale (one fp32 rounding), then to the
+// activation dtype (round to nearest even).
+template <int DT>
+__device__ __forceinline__ uint32_t ref_pair(uint2 lv, float s) {
+  unsigned long long t, ss, r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(t) : "r"(lv.x), "r"(lv.y));
+  asm("mov.b64 %0, {%1,%1};" : "=l"(ss) : "f"(s));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(t), "l"(ss));
+  float lo, hi;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  uint32_t d;
+  if constexpr (DT == RQ_BF16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 template <int DT, int MG>
 __device__ __forceinline__ void kstep(float (&part)[MG][4], bool first, uint32_t a0, uint32_t a1, uint32_t a2,
                                       uint32_t a3, const uint32_t (&x)[MG][8], int j) {
@@ -349,36 +370,29 @@ __host__ __device__ __forceinline__ int mma_row(int g, int wide) { return wide ?
 // MMA row of tile row rr (0..15) modulo 8
 __host__ __device__ __forceinline__ int mma_of_row(int rr, int wide) { return wide ? (rr & 7) : ((rr & 7) >> 1) + 4 * (rr & 1); }
 
-template <int DT, int MG, int NT>
+template <int DT, int MG, int NT, bool EXACT>
 __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_constant__ Nf4Args q) {
   using T = typename DType<DT>::T;
   const GemvArgs& p = q.a;
   extern __shared__ __align__(16) unsigned char smem[];
-  // full[S] (TMA bytes), empty[S] (consumer warps), decoded[S] (one arrival
-  // per decoder warp), raw scales of a pass full / empty (the decoders
-  // release it)
-  __shared__ __align__(8) uint64_t bars[3 * kNfMaxSlots + 2];
+  __shared__ __align__(8) uint64_t bars[2 * kNfMaxSlots + 2];  // full[S], empty[S], scales full / empty
   __shared__ int abort_flag, issued, raw_issued, producer_done, stop, gather_skip;
   __shared__ uint32_t gather_epoch;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  // Behind the down-product kernel (early): the next layer's down product (a
-  // programmatic dependent, which waits for this grid to finish before it
-  // reads anything or lets its own dependent start) may be scheduled beside
-  // this grid now.  Otherwise the dependents are released only after this
-  // grid's own griddepcontrol.wait (below), so that a dependent that reads
-  // its weights before its wait only ever follows finished kernels.
-  if (q.early) asm volatile("griddepcontrol.launch_dependents;");
+  // The next layer's down-product kernel (a programmatic dependent) may be
+  // scheduled beside this grid now: it waits for this grid to finish before
+  // it reads anything or lets its own dependent start.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
   const int nbk = K >> 6;
   const int nst = (nbk + kStageBlocks - 1) / kStageBlocks;
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
   const uint32_t ring = (sbase + q.ring_off + 1023u) & ~1023u;  // shared address (swizzle atoms are 1 KB)
-  const int S = q.slots;
+  const int sp = q.sp, S = q.slots;
   const uint32_t slot_bytes = q.slot_bytes;
   constexpr uint32_t kBox = NT * 16 * 128;  // one 128-byte-wide code box
   const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(bars), empty0 = full0 + kNfMaxSlots * 8;
-  const uint32_t dec0 = full0 + 2 * kNfMaxSlots * 8;
-  const uint32_t scfull = full0 + 3 * kNfMaxSlots * 8, scempty = scfull + 8;
+  const uint32_t scfull = full0 + 2 * kNfMaxSlots * 8, scempty = scfull + 8;
   // raw scale bytes of the pass at rows [c0, c0+R): one copy of the 16-byte
   // aligned part (the rest, under 16 bytes, is read directly)
   const int esz = q.esz;
@@ -396,9 +410,9 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     t1 = t0 + NT < te ? t0 + NT : te;
   };
 
-  if (warp == kNfWarps + kNfDecWarps) {
+  if (warp == kNfWarps) {
     // ---- producer: initializes the mbarriers and flags itself and starts
-    // issuing at once; the other warps wait for its start signal only before
+    // issuing at once; the consumers wait for its start signal only before
     // their first mbarrier wait (their table builds run meanwhile)
     if (lane == 0) {
       // every kernel parameter the issue path reads, loaded at once: the
@@ -410,7 +424,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       for (int i = 0; i < S; ++i) {
         mbar_init(full0 + 8 * i, 1);
         mbar_init(empty0 + 8 * i, kNfWarps);
-        mbar_init(dec0 + 8 * i, kNfDecWarps);
       }
       mbar_init(scfull, 1);
       mbar_init(scempty, 1);
@@ -422,22 +435,16 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     }
     __syncwarp();
     start_arrive();
-    if (!q.early) {
-      // every kernel before this one has finished (and its memory is
-      // visible) from here on; only now may this grid's dependents start
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      asm volatile("griddepcontrol.launch_dependents;");
-    }
     // ---- stage u (over all passes) into slot u % S
     if (lane == 0) {
       const uint32_t bytes = 2 * kBox + (uint32_t)M * 1024;
-      uint32_t u = 0, slot = 0, round = 0;  // u % S and u / S
+      uint32_t u = 0;
       for (int ch = 0; ch < q.chunks && !*abortp; ++ch) {
         int t0, t1;
         pass_tiles(ch, t0, t1);
         if (t1 <= t0) break;
-        // the pass's raw scales first (the buffer is free once the decoders
-        // are done with the previous pass's)
+        // the pass's raw scales first (the buffer is free once the consumers
+        // decoded the previous pass's)
         if (ch > 0 && !mbar_wait(scempty, (ch - 1) & 1, abortp)) break;
         const int R = (t1 * 16 < N ? t1 * 16 : N) - t0 * 16;
         const uint32_t rb = raw_bytes(R);
@@ -452,7 +459,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
                     scfull);
         *raw_issuedp = ch + 1;
         for (int s = 0; s < nst; ++s, ++u) {
-          if (round > 0 && !mbar_wait(empty0 + 8 * slot, (round - 1) & 1, abortp)) break;
+          const uint32_t slot = u % S;
+          if (u >= (uint32_t)S && !mbar_wait(empty0 + 8 * slot, ((u / S) - 1) & 1, abortp)) break;
           const uint32_t dst = ring + slot * slot_bytes, bar = full0 + 8 * slot;
           mbar_expect_tx(bar, bytes);
           if (q.wide) {
@@ -463,7 +471,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           }
           tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
           *issuedp = (int)(u + 1);
-          if (++slot == (uint32_t)S) slot = 0, ++round;
         }
       }
       __threadfence_block();
@@ -472,100 +479,13 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     return;
   }
 
-  const int fmt = p.w.fmt;
-  const unsigned char* raw = smem + q.raw_off;
-  float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
-  float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
-  const int wide = q.wide;
-
-  if (warp >= kNfWarps) {
-    // ---- scale decoders: per stage, the block scales of the pass's rows for
-    // the stage's 8 blocks (fp8 / int8 second level times c2_scales, or the
-    // plain per-block scales) into the slot, in fragment order
-    // [block][tile][MMA row g][rows g, g + 8]; then one arrival per warp on
-    // the slot's decoded barrier (the consumers wait for it and for the
-    // slot's TMA bytes).  Thread d takes block d % 8 of the stage and the pass
-    // rows d / 8 + 8 i.
-    const int d = tid - kNfThreads;
-    if (fmt != RQ_W_NF4)
-      for (int i = d; i < 256; i += kNfDecThreads)
-        sclut[i] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(i) : ieee_div((float)(int8_t)i, 127.0f);
-    start_wait();  // the producer's mbarriers and flags are initialized
-    const int bb = d & 7, r0 = d >> 3;
-    uint32_t u = 0, slot = 0, round = 0;
-    for (int ch = 0; ch < q.chunks; ++ch) {
-      int t0, t1;
-      pass_tiles(ch, t0, t1);
-      if (t1 <= t0) break;
-      const int c0 = t0 * 16;
-      const int R = (t1 * 16 < N ? t1 * 16 : N) - c0;
-      const int64_t f0 = (int64_t)c0 * nbk;
-      const int f0lo = (int)(f0 & 255), inraw = (int)(raw_bytes(R) / esz);
-      if (fmt != RQ_W_NF4) {  // the pass's c2_scales (one per 256 blocks)
-        dec_sync();           // the previous pass's are no longer read
-        const int n = (int)(((f0 + (int64_t)R * nbk - 1) >> 8) - (f0 >> 8)) + 1;
-        for (int i = d; i < n; i += kNfDecThreads) c2s_sm[i] = __ldg(p.w.c2s + (f0 >> 8) + i);
-        dec_sync();
-      }
-      // (the two decoder warps take the same barrier sequence whatever
-      // happens: a wait that gives up only skips work, every later wait then
-      // returns at once)
-      bool ok = mbar_wait(scfull, ch & 1, abortp);
-      for (int s = 0; s < nst; ++s, ++u) {
-        ok = ok && (round == 0 || mbar_wait(empty0 + 8 * slot, (round - 1) & 1, abortp));
-        if (!ok) {
-          if (++slot == (uint32_t)S) slot = 0, ++round;
-          continue;
-        }
-        float* dst = reinterpret_cast<float*>(smem + (ring - sbase) + slot * slot_bytes + q.scl_off);
-        const int b = s * kStageBlocks + bb;
-        if (b < nbk) {
-          // all of the thread's loads first, then the lookups and stores:
-          // 2 NT independent chains instead of one after the other
-          float v[2 * NT];
-          if (fmt == RQ_W_NF4) {
-#pragma unroll
-            for (int k = 0; k < 2 * NT; ++k) {
-              const int rl = r0 + 8 * k, e = rl * nbk + b;
-              v[k] = rl >= R ? 0.0f
-                     : e < inraw ? (esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e))
-                                 : load_scalar(p.w.scales, p.w.sdt, f0 + e);
-            }
-          } else {
-            uint32_t cb[2 * NT];
-#pragma unroll
-            for (int k = 0; k < 2 * NT; ++k) {
-              const int rl = r0 + 8 * k, e = rl * nbk + b;
-              cb[k] = rl >= R ? 0u : e < inraw ? (uint32_t)raw[e] : (uint32_t)__ldg(p.w.c2 + f0 + e);
-            }
-#pragma unroll
-            for (int k = 0; k < 2 * NT; ++k) {
-              const int rl = r0 + 8 * k, e = rl * nbk + b;
-              v[k] = rl >= R ? 0.0f : sclut[cb[k]] * c2s_sm[(f0lo + e) >> 8];
-            }
-          }
-#pragma unroll
-          for (int k = 0; k < 2 * NT; ++k) {
-            const int rl = r0 + 8 * k, rr = rl & 15;
-            dst[(bb * NT + (rl >> 4)) * 16 + mma_of_row(rr, wide) * 2 + (rr >> 3)] = v[k];
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dec0 + 8 * slot);
-        if (++slot == (uint32_t)S) slot = 0, ++round;
-      }
-      // both decoder warps are done with this pass's raw scales
-      dec_sync();
-      if (d == 0) mbar_arrive(scempty);
-    }
-    return;
-  }
-
   // ---- consumers
   unsigned char* lut = smem;
+  float* sc = reinterpret_cast<float*>(smem + q.sc_off);
+  float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
   T* tl = reinterpret_cast<T*>(smem + q.tl_off);
   T* stg = reinterpret_cast<T*>(smem + q.stg_off);
-  const uint32_t lanesel = sbase + (uint32_t)(lane * 4);
+  const uint32_t lanesel = sbase + (uint32_t)(lane * (EXACT ? 8 : 4));
   // warp pair bw = warp % 8 multiplies block bw of each stage; warp bw + 8 h
   // takes the pass's tiles nt = h, h + 2, ...
   const int bw = warp % kStageBlocks, th = warp / kStageBlocks;
@@ -574,6 +494,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   // the 128-byte shared rows are swizzled by their index mod 8.
   //   3-D: shared row 2*r + half -> per tile 4096 bytes, per h 2048
   //   2-D: half at kBox, shared row r -> per tile 2048 bytes, per h 1024
+  const int wide = q.wide;
   const int pg = mma_row(g, wide), half = bw >> 2, lch = 2 * (bw & 3) + (t >> 1);
   // (a tile is 16 or 32 shared rows: the swizzle phase repeats per tile)
   const uint32_t tstep = wide ? 4096u : 2048u, hstep = tstep / 2;
@@ -588,12 +509,72 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     const int m = gr * 8 + g;
     xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + bw * 128 + t * 32;
   }
-  // lane's scales in a slot: block bw, tile th + 2 i, MMA row g (rows g, g + 8)
-  const uint32_t sofs = q.scl_off + (uint32_t)((bw * NT + th) * 16 + g * 2) * 4;
 
-  // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])),
-  // built while the first stages are in flight
-  {
+  // decoded scales of the pass at rows [c0, c0+R) into sc in fragment order
+  // [block][tile][MMA row g][g / g+8]
+  const int fmt = p.w.fmt;
+  const unsigned char* raw = smem + q.raw_off;
+  float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
+  auto c2s_load = [&](int c0, int R) {  // the pass's c2_scales (one per 256 blocks)
+    if (fmt == RQ_W_NF4) return;
+    const int64_t f0 = (int64_t)c0 * nbk;
+    const int n = (int)(((f0 + (int64_t)R * nbk - 1) >> 8) - (f0 >> 8)) + 1;
+    for (int i = tid; i < n; i += kNfThreads) c2s_sm[i] = __ldg(p.w.c2s + (f0 >> 8) + i);
+  };
+  auto decode = [&](int c0, int R) {
+    const int64_t f0 = (int64_t)c0 * nbk;
+    const int total = R * nbk, inraw = (int)(raw_bytes(R) / esz);
+    // entry e = rl * nbk + b (row rl of the pass, block b), stepped by
+    // kNfThreads without a division per entry; its c2_scales entry is
+    // (f0 % 256 + e) / 256 of the pass's
+    const int f0lo = (int)(f0 & 255), dq = kNfThreads / nbk, dr = kNfThreads - dq * nbk;
+    int rl = tid / nbk, b = tid - rl * nbk;
+    auto put = [&](float v) {
+      const int rr = rl & 15, gg = mma_of_row(rr, q.wide);
+      sc[b * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = v;
+      b += dr;
+      rl += dq;
+      if (b >= nbk) b -= nbk, ++rl;
+    };
+    // the entries in the shared copy, then the tail (under 16 bytes) from
+    // global memory: separate loops, so that no shared entry waits on a
+    // global load the compiler would otherwise issue for every entry
+    int e = tid;
+    if (fmt == RQ_W_NF4) {
+      for (; e < inraw; e += kNfThreads)
+        put(esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e));
+      for (; e < total; e += kNfThreads) put(load_scalar(p.w.scales, p.w.sdt, f0 + e));
+    } else {
+      // four entries a thread per round, their loads ahead of the stores
+      // (four independent load chains instead of one)
+      for (; e + 3 * kNfThreads < inraw; e += 4 * kNfThreads) {
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = sclut[raw[e + i * kNfThreads]] * c2s_sm[(f0lo + e + i * kNfThreads) >> 8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) put(v[i]);
+      }
+      for (; e < inraw; e += kNfThreads) put(sclut[raw[e]] * c2s_sm[(f0lo + e) >> 8]);
+      for (; e < total; e += kNfThreads) put(sclut[__ldg(p.w.c2 + f0 + e)] * c2s_sm[(f0lo + e) >> 8]);
+    }
+  };
+
+  int t0, t1;
+  pass_tiles(0, t0, t1);
+  if (t1 > t0) c2s_load(t0 * 16, (t1 * 16 < N ? t1 * 16 : N) - t0 * 16);
+  // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])) and
+  // the second-level table, built while the first stages are in flight
+  if constexpr (EXACT) {
+    // entry v: 32 copies of the fp32 pair (T[v & 15], T[v >> 4]), 8 bytes a lane
+    const float lvl = nf4_level_imm(lane & 15);
+#pragma unroll 1
+    for (int k = 0; k < 256 * 16 / kNfThreads; ++k) {
+      const int v = k * (kNfThreads / 16) + (tid >> 4);
+      const uint32_t a = __float_as_uint(__shfl_sync(0xffffffffu, lvl, v & 15));
+      const uint32_t b = __float_as_uint(__shfl_sync(0xffffffffu, lvl, v >> 4));
+      *reinterpret_cast<uint4*>(lut + v * 256 + (tid & 15) * 16) = make_uint4(a, b, a, b);
+    }
+  } else {
     const float lvl = nf4_level_imm(lane & 15);
 #pragma unroll 1
     for (int k = 0; k < 256 * 8 / kNfThreads; ++k) {
@@ -602,23 +583,30 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       *reinterpret_cast<uint4*>(lut + v * 128 + (tid & 7) * 16) = make_uint4(w, w, w, w);
     }
   }
+  if (fmt != RQ_W_NF4 && tid < 256)
+    sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
   if (p.gather && tid == 0) {
-    // the entry announcement follows every earlier kernel of this stream
-    if (!q.early) asm volatile("griddepcontrol.wait;" ::: "memory");
     gather_epoch = gather_enter(p.gth);
     gather_skip = 0;
   }
 
   start_wait();  // the producer's mbarriers and flags are initialized
-  consumer_sync();  // the code table is complete
   uint32_t u = 0;       // stages consumed (over all passes)
   uint32_t cslot = 0, cphase = 0;  // u % S and (u / S) & 1, kept without divisions
-  int t0, t1;
+  uint32_t passes = 0;  // raw-scale copies waited for
   for (int ch = 0; ch < q.chunks; ++ch) {
-    pass_tiles(ch, t0, t1);
+    if (ch > 0) pass_tiles(ch, t0, t1);
     if (t1 <= t0) break;
     const int ntl = t1 - t0, c0 = t0 * 16;
     const int R = (t1 * 16 < N ? t1 * 16 : N) - c0;
+    if (ch > 0) c2s_load(c0, R);
+    consumer_sync();  // tables and c2_scales in place
+    // the pass's raw scales have landed: decode them, then hand the buffer back
+    mbar_wait(scfull, ch & 1, abortp);
+    ++passes;
+    decode(c0, R);
+    consumer_sync();
+    if (tid == 0) mbar_arrive(scempty);
 
     // this warp's tiles: nt = th + kNfSplit * i for i < NTW (nt < NT)
     constexpr int NTW = (NT + kNfSplit - 1) / kNfSplit;
@@ -627,10 +615,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     for (int i = 0; i < NTW; ++i)
 #pragma unroll
       for (int gr = 0; gr < MG; ++gr) acc[i][gr][0] = acc[i][gr][1] = acc[i][gr][2] = acc[i][gr][3] = 0.0f;
+    const float* scw = sc + bw * sp + th * 16 + g * 2;
 
     for (int s = 0; s < nst; ++s, ++u) {
       const uint32_t slot = cslot;
-      const bool ok = mbar_wait(full0 + 8 * slot, cphase, abortp) && mbar_wait(dec0 + 8 * slot, cphase, abortp);
+      const bool ok = mbar_wait(full0 + 8 * slot, cphase, abortp);
       const int b = s * kStageBlocks + bw;
       if (ok && b < nbk) {
         const uint32_t sl = ring + slot * slot_bytes;
@@ -643,6 +632,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           x[gr][0] = u0.x, x[gr][1] = u0.y, x[gr][2] = u0.z, x[gr][3] = u0.w;
           x[gr][4] = u1.x, x[gr][5] = u1.y, x[gr][6] = u1.z, x[gr][7] = u1.w;
         }
+        const float* sb = scw + (size_t)s * kStageBlocks * sp;
 #pragma unroll
         for (int i = 0; i < NTW; ++i) {
           const int nt = th + kNfSplit * i;
@@ -650,17 +640,36 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           uint2 lo, hi;
           asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + i * kNfSplit * tstep));
           asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + i * kNfSplit * tstep + hstep));
-          float2 sv;
-          asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(sv.x), "=f"(sv.y) : "r"(sl + sofs + i * kNfSplit * 64));
+          const float2 sv = *reinterpret_cast<const float2*>(sb + i * kNfSplit * 16);
           float part[MG][4];
-          kstep<DT, MG>(part, true, lut2<0>(lo.x, lanesel), lut2<0>(hi.x, lanesel), lut2<1>(lo.x, lanesel),
-                        lut2<1>(hi.x, lanesel), x, 0);
-          kstep<DT, MG>(part, false, lut2<2>(lo.x, lanesel), lut2<2>(hi.x, lanesel), lut2<3>(lo.x, lanesel),
-                        lut2<3>(hi.x, lanesel), x, 1);
-          kstep<DT, MG>(part, false, lut2<0>(lo.y, lanesel), lut2<0>(hi.y, lanesel), lut2<1>(lo.y, lanesel),
-                        lut2<1>(hi.y, lanesel), x, 2);
-          kstep<DT, MG>(part, false, lut2<2>(lo.y, lanesel), lut2<2>(hi.y, lanesel), lut2<3>(lo.y, lanesel),
-                        lut2<3>(hi.y, lanesel), x, 3);
+          if constexpr (EXACT) {
+            // the reference's weights (level x scale, rounded), multiplied
+            // straight into the accumulators: no per-block scale step
+            const float sg = sv.x, sg8 = sv.y;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t wlo = j < 2 ? lo.x : lo.y, whi = j < 2 ? hi.x : hi.y;
+              const uint2 l0 = (j & 1) ? lut4<2>(wlo, lanesel) : lut4<0>(wlo, lanesel);
+              const uint2 h0 = (j & 1) ? lut4<2>(whi, lanesel) : lut4<0>(whi, lanesel);
+              const uint2 l1 = (j & 1) ? lut4<3>(wlo, lanesel) : lut4<1>(wlo, lanesel);
+              const uint2 h1 = (j & 1) ? lut4<3>(whi, lanesel) : lut4<1>(whi, lanesel);
+              const uint32_t a0 = ref_pair<DT>(l0, sg), a1 = ref_pair<DT>(h0, sg8);
+              const uint32_t a2 = ref_pair<DT>(l1, sg), a3 = ref_pair<DT>(h1, sg8);
+#pragma unroll
+              for (int gr = 0; gr < MG; ++gr) Mma16816<DT>::run(acc[i][gr], a0, a1, a2, a3, x[gr][2 * j], x[gr][2 * j + 1]);
+            }
+            (void)part;
+            continue;
+          } else {
+            kstep<DT, MG>(part, true, lut2<0>(lo.x, lanesel), lut2<0>(hi.x, lanesel), lut2<1>(lo.x, lanesel),
+                          lut2<1>(hi.x, lanesel), x, 0);
+            kstep<DT, MG>(part, false, lut2<2>(lo.x, lanesel), lut2<2>(hi.x, lanesel), lut2<3>(lo.x, lanesel),
+                          lut2<3>(hi.x, lanesel), x, 1);
+            kstep<DT, MG>(part, false, lut2<0>(lo.y, lanesel), lut2<0>(hi.y, lanesel), lut2<1>(lo.y, lanesel),
+                          lut2<1>(hi.y, lanesel), x, 2);
+            kstep<DT, MG>(part, false, lut2<2>(lo.y, lanesel), lut2<2>(hi.y, lanesel), lut2<3>(lo.y, lanesel),
+                          lut2<3>(hi.y, lanesel), x, 3);
+          }
 #pragma unroll
           for (int gr = 0; gr < MG; ++gr) {
             fma2(acc[i][gr][0], acc[i][gr][1], part[gr][0], part[gr][1], sv.x);
@@ -673,8 +682,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       if (++cslot == (uint32_t)S) cslot = 0, cphase ^= 1u;
     }
 
-    // with one pass, LoRA B's rows came with the pass's raw scales
-    if (ch == 0 && q.bsm) mbar_wait(scfull, 0, abortp);
     consumer_sync();  // every warp is done with the ring (the partial sums may reuse it)
     if (tid == 0) stop = *abortp;  // one decision for all consumers (the producer may set the flag any time)
     consumer_sync();
@@ -779,9 +786,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     for (uint32_t v = u; v < n; ++v)
       for (uint32_t i = 0; i < kWaitLimit && !mbar_test(full0 + 8 * (v % S), (v / S) & 1); ++i) {
       }
-    // raw-scale copies complete in order: the last one issued covers all
-    if (nr > 0)
-      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, (nr - 1) & 1); ++i) {
+    for (uint32_t v = passes; v < nr; ++v)
+      for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, v & 1); ++i) {
       }
   }
   if (p.gather) {
@@ -878,19 +884,19 @@ int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64
 }
 
 struct Nf4Plan {
-  int grid, tiles, tpc, chunks, nt, mg, esz, slots;
+  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
   size_t smem;
-  uint32_t slot_bytes, scl_off, ring_off, red_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
+  uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
 };
 
-// [code table | raw scales + c2_scales of a pass | second-level table |
-// x.A^T | staged outputs | LoRA B rows | ring (1 KB aligned) | partial
-// sums]; a slot is [codes | X | the stage's decoded scales]; with one pass
-// the partial sums reuse the ring.
-static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
-  pl->scl_off = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
-  pl->slot_bytes = (pl->scl_off + (uint32_t)pl->nt * 512 + 1023u) & ~1023u;
-  size_t off = kLutBytes;
+// [code table | scales | raw scales + c2_scales of a pass | second-level
+// table | x.A^T | staged outputs | ring (1 KB aligned) | partial sums];
+// with one pass the partial sums reuse the ring.
+static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r, bool exact) {
+  pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
+  size_t off = lut_bytes(exact);
+  pl->sc_off = (uint32_t)off;
+  off += align16((size_t)nbk * pl->sp * 4);
   pl->raw_off = (uint32_t)off;
   off += align16((size_t)pl->nt * 16 * nbk * pl->esz) + align16(((size_t)pl->nt * 16 * nbk / 256 + 2) * 4);
   pl->aux_off = (uint32_t)off;
@@ -914,7 +920,7 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r) {
   return pl->smem;
 }
 
-static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool pdl, Nf4Plan* pl) {
+static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool pdl, bool exact, Nf4Plan* pl) {
   pl->mg = M > 8 ? 2 : 1;
   pl->esz = esz;
   const int64_t tiles = (N + 15) / 16;
@@ -932,12 +938,11 @@ static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool pdl, 
     pl->nt = (int)nt;
     pl->tpc = (int)(nt * ch);
     pl->grid = (int)((tiles + pl->tpc - 1) / pl->tpc);
-    // deepest ring that fits (at least 2 stages; no more than the stages of
-    // all passes)
-    const int64_t all = nst * ch;
-    for (int s = (int)(all < kNfMaxSlots ? (all > 2 ? all : 2) : kNfMaxSlots); s >= 2; --s) {
+    // deepest ring that fits (at least 2 stages)
+    pl->sp = (int)(nt * 16 + 2);
+    for (int s = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots); s >= 2; --s) {
       pl->slots = s;
-      if (nf4_layout(pl, nbk, M, r) <= kNfSmemMax) return true;
+      if (nf4_layout(pl, nbk, M, r, exact) <= kNfSmemMax) return true;
     }
     if (nt == 1) return false;
   }
@@ -949,16 +954,37 @@ static int nf4_esz(const QWeight& w) {
   return w.sdt == RQ_F32 ? 4 : 2;
 }
 
+// Decode numerics: 0 = levels rounded once to the activation dtype, the
+// block scale applied to each 64-wide fp32 partial (the default); 1 = the
+// reference's weights, level x scale rounded per weight (exact mode).
+// RQ_DECODE_EXACT=1 in the environment selects 1 at the first call;
+// rq_set_decode_exact() changes it at any time.
+static std::atomic<int> g_decode_exact{-1};
+
+bool decode_exact() {
+  int v = g_decode_exact.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = getenv("RQ_DECODE_EXACT");
+    v = (e && e[0] == '1') ? 1 : 0;
+    int expected = -1;
+    if (!g_decode_exact.compare_exchange_strong(expected, v)) v = expected;
+  }
+  return v == 1;
+}
+
+void set_decode_exact(int on) { g_decode_exact.store(on ? 1 : 0); }
+
 bool gemv_nf4_fits(const QWeight& w, int64_t M, int r) {
   Nf4Plan pl;
   const void* sp = w.fmt == RQ_W_NF4 ? w.scales : (const void*)w.c2;
-  return encode_tiled() != nullptr && ((uintptr_t)sp % 16) == 0 && nf4_plan(w.N, w.K, M, r, nf4_esz(w), false, &pl) &&
-         nf4_plan(w.N, w.K, M, r, nf4_esz(w), true, &pl);
+  const bool exact = decode_exact();
+  return encode_tiled() != nullptr && ((uintptr_t)sp % 16) == 0 &&
+         nf4_plan(w.N, w.K, M, r, nf4_esz(w), false, exact, &pl) && nf4_plan(w.N, w.K, M, r, nf4_esz(w), true, exact, &pl);
 }
 
-template <int DT, int MG, int NT>
+template <int DT, int MG, int NT, bool EXACT>
 static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) {
-  auto kern = gemv_nf4_k<DT, MG, NT>;
+  auto kern = gemv_nf4_k<DT, MG, NT, EXACT>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -970,8 +996,7 @@ static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) 
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;  // early or not, the kernel waits (griddepcontrol.wait) before reading what others wrote
-  (void)pdl;
+  cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q);
   if (e != cudaSuccess) {
     set_cuda_error(e);
@@ -980,24 +1005,30 @@ static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) 
   return check_launch();
 }
 
-template <int DT, int MG>
+template <int DT, int MG, bool EXACT>
 static int nf4_nt(const Nf4Args& q, int nt, size_t smem, bool pdl, cudaStream_t st) {
   switch (nt) {
-    case 1: return nf4_launch<DT, MG, 1>(q, smem, pdl, st);
-    case 2: return nf4_launch<DT, MG, 2>(q, smem, pdl, st);
-    case 3: return nf4_launch<DT, MG, 3>(q, smem, pdl, st);
-    case 4: return nf4_launch<DT, MG, 4>(q, smem, pdl, st);
-    case 5: return nf4_launch<DT, MG, 5>(q, smem, pdl, st);
+    case 1: return nf4_launch<DT, MG, 1, EXACT>(q, smem, pdl, st);
+    case 2: return nf4_launch<DT, MG, 2, EXACT>(q, smem, pdl, st);
+    case 3: return nf4_launch<DT, MG, 3, EXACT>(q, smem, pdl, st);
+    case 4: return nf4_launch<DT, MG, 4, EXACT>(q, smem, pdl, st);
+    case 5: return nf4_launch<DT, MG, 5, EXACT>(q, smem, pdl, st);
   }
   if constexpr (MG == 1)
-    if (nt == 6) return nf4_launch<DT, MG, 6>(q, smem, pdl, st);
+    if (nt == 6) return nf4_launch<DT, MG, 6, EXACT>(q, smem, pdl, st);
   return RQ_ERR_INVALID;
+}
+
+template <int DT, bool EXACT>
+static int nf4_dispatch(const Nf4Args& q, const Nf4Plan& pl, bool pdl, cudaStream_t st) {
+  return pl.mg == 2 ? nf4_nt<DT, 2, EXACT>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<DT, 1, EXACT>(q, pl.nt, pl.smem, pdl, st);
 }
 
 int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   if (g.w.K % 64 || ((uintptr_t)g.w.q % 16) || ((uintptr_t)g.x % 16)) return RQ_ERR_ALIGN;
   Nf4Plan pl;
-  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), pdl, &pl)) return RQ_ERR_INVALID;
+  const bool exact = decode_exact();
+  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), pdl, exact, &pl)) return RQ_ERR_INVALID;
   Nf4Args q;
   // codes with 128-byte swizzle: 3-D [N][K/256][128] bytes, box 128 x 2 x NT*16
   // when K % 256 == 0, else 2-D [N][K/2] bytes, box 128 x NT*16;
@@ -1020,13 +1051,13 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   q.tiles = pl.tiles;
   q.tpc = pl.tpc;
   q.chunks = pl.chunks;
+  q.sp = pl.sp;
   q.esz = pl.esz;
   q.slots = pl.slots;
   q.slot_bytes = pl.slot_bytes;
   q.ring_off = pl.ring_off;
   q.red_off = pl.red_off;
-  q.scl_off = pl.scl_off;
-  q.early = pdl ? 1 : 0;
+  q.sc_off = pl.sc_off;
   q.raw_off = pl.raw_off;
   q.aux_off = pl.aux_off;
   q.tl_off = pl.tl_off;
@@ -1034,8 +1065,8 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   q.bsm_off = pl.bsm_off;
   q.bsm = pl.chunks == 1 && g.r > 0 && g.r % 8 == 0 && ((uintptr_t)g.lora_b % 16) == 0;
   if (g.xdt == RQ_BF16)
-    return pl.mg == 2 ? nf4_nt<RQ_BF16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_BF16, 1>(q, pl.nt, pl.smem, pdl, st);
-  return pl.mg == 2 ? nf4_nt<RQ_F16, 2>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<RQ_F16, 1>(q, pl.nt, pl.smem, pdl, st);
+    return exact ? nf4_dispatch<RQ_BF16, true>(q, pl, pdl, st) : nf4_dispatch<RQ_BF16, false>(q, pl, pdl, st);
+  return exact ? nf4_dispatch<RQ_F16, true>(q, pl, pdl, st) : nf4_dispatch<RQ_F16, false>(q, pl, pdl, st);
 }
 
 }  // namespace rq

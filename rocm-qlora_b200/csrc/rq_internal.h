@@ -12,6 +12,9 @@ namespace rq {
 // Kernel family of the last layer call in this thread (RQ_PATH_*).
 int last_path();
 
+// Decode GEMV numerics (rq_set_decode_exact; gemv_nf4.cu).
+void set_decode_exact(int on);
+
 // Records the CUDA error of the last failing launch in this thread.
 void set_cuda_error(cudaError_t e);
 

@@ -57,6 +57,7 @@ def _bind(L: ctypes.CDLL) -> None:
         "rq_last_cuda_error": ([], I),
         "rq_last_status": ([], I),
         "rq_last_path": ([], I),
+        "rq_set_decode_exact": ([I], None),
         "rq_take_kernel_timeouts": ([P], I),
         "rq_nf4_quantize": ([P, I, I64, I, P, P, P], I),
         "rq_nf4_dequantize": ([P, I64, P, I, I, P, I, P], I),
@@ -88,6 +89,7 @@ def _bind(L: ctypes.CDLL) -> None:
 def exported_symbols() -> Tuple[str, ...]:
     """Names of the C entry points this binding declares."""
     return ("rq_abi_version", "rq_status_string", "rq_last_cuda_error", "rq_last_status", "rq_last_path",
+            "rq_set_decode_exact",
             "rq_take_kernel_timeouts",
             "rq_nf4_quantize", "rq_nf4_dequantize", "rq_int8_quantize", "rq_int8_quantize_rows",
             "rq_int8_dequantize", "rq_dq_quantize_scales", "rq_dq_dequantize",
@@ -201,3 +203,12 @@ def workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) -
 
 def lib() -> ctypes.CDLL:
     return _lib_for_compute()
+
+
+def set_decode_exact(exact: bool) -> None:
+    """Decode GEMV numerics for later calls: False (default) rounds each NF4
+    level once to the activation dtype and applies the block scale to fp32
+    partial sums; True forms the reference's own weights (level x scale,
+    rounded per weight), so only the summation order separates the results
+    (slower).  Same as RQ_DECODE_EXACT=1 in the environment."""
+    load_library().rq_set_decode_exact(1 if exact else 0)

@@ -29,12 +29,18 @@ def _need_gpu():
 
 
 class Block(nn.Module):
-    def __init__(self, d, f):
+    """Attention-shaped projections and an MLP: SwiGLU (gate/up/down, as in
+    Llama; the down projection sees centred activations) or ReLU (the down
+    projection sees activations that all share a sign)."""
+
+    def __init__(self, d, f, relu):
         super().__init__()
+        self.relu = relu
         self.q_proj = nn.Linear(d, d, bias=False)
         self.k_proj = nn.Linear(d, d, bias=False)
         self.v_proj = nn.Linear(d, d, bias=True)
         self.o_proj = nn.Linear(d, d, bias=False)
+        self.gate_proj = nn.Linear(d, f, bias=False)
         self.up_proj = nn.Linear(d, f, bias=False)
         self.down_proj = nn.Linear(f, d, bias=False)
         self.norm = nn.LayerNorm(d)
@@ -42,13 +48,14 @@ class Block(nn.Module):
     def forward(self, x):
         h = self.o_proj(self.q_proj(x) + self.k_proj(x) + self.v_proj(x))
         x = self.norm(x + h)
-        return x + self.down_proj(torch.relu(self.up_proj(x)))
+        a = torch.relu(self.up_proj(x)) if self.relu else nn.functional.silu(self.gate_proj(x)) * self.up_proj(x)
+        return x + self.down_proj(a)
 
 
 class TinyModel(nn.Module):
-    def __init__(self, d=256, f=512, n=3):
+    def __init__(self, d=256, f=512, n=3, relu=False):
         super().__init__()
-        self.blocks = nn.ModuleList([Block(d, f) for _ in range(n)])
+        self.blocks = nn.ModuleList([Block(d, f, relu) for _ in range(n)])
         self.tiny = nn.Linear(32, 32)   # below quantize_model's 64-feature floor
         self.head = nn.Linear(d, 64)    # not a target
 
@@ -58,7 +65,15 @@ class TinyModel(nn.Module):
         return self.head(x)
 
 
-TARGETS = ["q_proj", "k_proj", "v_proj", "o_proj", "up_proj", "down_proj"]
+TARGETS = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+
+
+@pytest.fixture
+def decode_mode():
+    """Sets the decode GEMV numerics for one test and restores the default."""
+    from rocm_qlora import _native as nat
+    yield nat.set_decode_exact
+    nat.set_decode_exact(False)
 
 
 def _taps(model):
@@ -70,15 +85,23 @@ def _taps(model):
     return seen, hooks
 
 
-@pytest.mark.parametrize("bits", [4, 8])
-@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
-def test_quantize_model_forward_backward(bits, dt):
+# (bits, dtype, ReLU MLP, exact decode numerics): the ReLU model runs the
+# decode GEMV with the exact numerics (the reference's own weights), meant
+# for activations that share a sign; the SwiGLU model runs the default
+CASES = [(4, torch.bfloat16, False, False), (8, torch.bfloat16, False, False), (4, torch.float32, False, False),
+         (8, torch.float32, False, False), (4, torch.bfloat16, True, True), (4, torch.float16, True, True)]
+
+
+@pytest.mark.parametrize("bits,dt,relu,exact", CASES)
+def test_quantize_model_forward_backward(bits, dt, relu, exact, decode_mode):
     from rocm_qlora import LoRALinear, QuantLinear, enable_all_kernels, quantize_model
+    decode_mode(exact)
     torch.manual_seed(bits)
-    model = TinyModel().to(device="cuda", dtype=dt)
-    model = quantize_model(model, bits=bits, lora_r=8, lora_alpha=16, lora_dropout=0.05, target_modules=TARGETS)
+    model = TinyModel(relu=relu).to(device="cuda", dtype=dt)
+    targets = [t for t in TARGETS if not (relu and t == "gate_proj")]
+    model = quantize_model(model, bits=bits, lora_r=8, lora_alpha=16, lora_dropout=0.05, target_modules=targets)
     n_swapped = sum(isinstance(m, LoRALinear) for m in model.modules())
-    assert n_swapped == 3 * len(TARGETS)
+    assert n_swapped == 3 * len(targets)
     assert isinstance(model.tiny, nn.Linear) and isinstance(model.head, nn.Linear)
     # like the reference's, the walk meets every QuantLinear twice: as the
     # LoRALinear's base_layer and as a module of its own
