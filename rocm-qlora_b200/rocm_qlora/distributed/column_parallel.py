@@ -16,6 +16,7 @@ layer is the fused B200 QuantLinear / LoRALinear of this package.  With
 all-gather: the GEMV writes its shard into every rank's output over NVLink
 and the ranks meet at the end of the kernel (``peer_gather.PeerGather``).
 """
+import math
 from typing import List, Optional, Tuple
 
 import torch
@@ -130,7 +131,8 @@ class ColumnParallelLinear(nn.Module):
         x2 = x2.contiguous()
         if isinstance(self.local, LoRALinear):
             base, dt = self.local.base_layer, x2.dtype
-            A, B, s = self.local.lora_A.to(dt).contiguous(), self.local.lora_B.to(dt).contiguous(), self.local.scaling
+            A, B = layer_ops.cast_param(self.local.lora_A, dt), layer_ops.cast_param(self.local.lora_B, dt)
+            s = self.local.scaling
         else:
             base, A, B, s = self.local, None, None, 1.0
         bias = base.bias.to(x2.dtype).contiguous() if base.bias is not None else None
@@ -187,3 +189,68 @@ class ColumnParallelLinear(nn.Module):
         return cls(local, linear.out_features, group=group, granule=granule, gather_tokens=gather_tokens,
                    gather_dtype=linear.weight.dtype if linear.weight.dtype in (torch.bfloat16, torch.float16)
                    else torch.bfloat16)
+
+    @classmethod
+    def from_quant_linear(cls, layer: nn.Module, group=None, granule: int = 16,
+                          gather_tokens: int = 0) -> "ColumnParallelLinear":
+        """Shards an already-quantized layer (a QuantLinear, or a LoRALinear
+        over one, holding the full weight on every rank -- e.g. loaded from a
+        checkpoint written by the reference) without re-quantizing: each rank
+        keeps its rows' codes and scales byte for byte.
+
+        Shard boundaries are rows r with r*K a multiple of the block size (no
+        block spans two shards) and, with double-quantized scales, r*K/64 a
+        multiple of the 256-block second-level group, so each shard's c2
+        bytes and c2_scales are a contiguous slice of the full layer's and
+        dequantize to exactly the same values (double_quant.py:46-97 of the
+        reference groups the flat block list in 256s).  LoRA B is sliced by
+        rows, LoRA A is kept whole (replicated)."""
+        world, rank = _world(group)
+        lora = layer if isinstance(layer, LoRALinear) else None
+        ql = lora.base_layer if lora is not None else layer
+        if not isinstance(ql, QuantLinear):
+            raise TypeError("from_quant_linear takes a QuantLinear or a LoRALinear over one")
+        N, K, bs = ql.out_features, ql.in_features, ql.block_size
+        dq = ql.bits == 4 and getattr(ql, "use_double_quant", False)
+        per_row = ql.bits == 8 and ql.weight_quant.dim() == 2 and ql.weight_scales.numel() == N
+        unit = granule
+        if not per_row:
+            unit = math.lcm(unit, bs // math.gcd(K, bs))  # whole blocks per shard
+        if dq:
+            bs2 = getattr(ql, "blocksize_2", 256)
+            unit = math.lcm(unit, (bs * bs2) // math.gcd(K, bs * bs2))  # whole second-level groups
+        lo, hi = shard_range(N, world, rank, unit)
+        local = QuantLinear(K, hi - lo, bits=ql.bits, bias=ql.bias is not None, block_size=bs)
+        local.original_shape = (hi - lo, K)
+        if per_row:
+            local.weight_quant = ql.weight_quant[lo:hi].clone()
+            local.weight_scales = ql.weight_scales.reshape(-1)[lo:hi].clone()
+        else:
+            per_byte = 2 if ql.bits == 4 else 1
+            b0, b1 = lo * K // bs, -(-(hi * K) // bs)
+            local.weight_quant = ql.weight_quant.reshape(-1)[b0 * bs // per_byte:b1 * bs // per_byte].clone()
+            if dq:
+                g0, g1 = b0 // bs2, -(-b1 // bs2)
+                local.register_buffer("c2", ql.c2.reshape(-1)[g0 * bs2:g1 * bs2].clone())
+                local.register_buffer("c2_scales", ql.c2_scales.reshape(-1)[g0:g1].clone())
+                local.blocksize_2 = bs2
+                local.use_fp8_c2 = getattr(ql, "use_fp8_c2", True)
+                local.use_double_quant = True
+                local.weight_scales = ql.weight_scales.new_empty(0)
+            else:
+                local.weight_scales = ql.weight_scales.reshape(-1)[b0:b1].clone()
+        if ql.bias is not None:
+            local.bias = ql.bias[lo:hi].clone()
+        local.use_triton_kernel = ql.use_triton_kernel
+        shard: nn.Module = local
+        if lora is not None:
+            shard = LoRALinear(local, r=lora.r, lora_alpha=lora.lora_alpha,
+                               lora_dropout=lora.lora_dropout.p if isinstance(lora.lora_dropout, nn.Dropout) else 0.0)
+            shard = shard.to(lora.lora_A.device)
+            with torch.no_grad():
+                shard.lora_A.copy_(lora.lora_A)
+                shard.lora_B.copy_(lora.lora_B[lo:hi])
+            shard.train(lora.training)
+        dtype = ql.bias.dtype if ql.bias is not None else torch.bfloat16
+        return cls(shard, N, group=group, granule=unit, gather_tokens=gather_tokens,
+                   gather_dtype=dtype if dtype in (torch.bfloat16, torch.float16) else torch.bfloat16)
