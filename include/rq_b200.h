@@ -158,6 +158,24 @@ RQ_API int rq_linear_dx(int wfmt, const void* qweight, const void* scales, int s
                  const void* lora_a, const void* lora_b, int r, float scaling,
                  void* dx, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The merged weight of a LoRA-adapted layer, dequantized and combined with
+ * the adapter in one pass over the codes:
+ *   out[n, k] = deq(W)[n, k] + scaling * sum_j lora_b[n, j] * lora_a[j, k]
+ * with lora_a [r, K] and lora_b [N, r] fp32 (the adapters' parameter dtype)
+ * and out [N, K] row-major in out_dtype.  mode RQ_MERGE_FP32_SUM adds in
+ * fp32 and rounds once (LoRALinear.merge_lora, rocm_qlora/lora/
+ * lora_layer.py:72-113); RQ_MERGE_ROUND_EACH rounds the weight and the delta
+ * to out_dtype first and adds them there (_export_dequant_layer,
+ * rocm_qlora/export/gguf_export.py:30-80).  r = 0 gives the dequantized
+ * weight alone (lora_a / lora_b may then be NULL).  r <= 128. */
+#define RQ_MERGE_FP32_SUM 0
+#define RQ_MERGE_ROUND_EACH 1
+RQ_API int rq_merge_lora(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                  const uint8_t* c2, const float* c2_scales,
+                  int64_t N, int64_t K, int block_size,
+                  const float* lora_a, const float* lora_b, int r, float scaling, int mode,
+                  void* out, int out_dtype, void* stream);
+
 /* Bytes of device scratch compiled into the library for
  * rq_linear_forward_noalloc (held on every GPU that loads the library). */
 #define RQ_NOALLOC_SCRATCH_BYTES (2u << 20)

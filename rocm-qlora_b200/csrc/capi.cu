@@ -264,6 +264,20 @@ int rq_linear_dx(int wfmt, const void* qweight, const void* scales, int scale_dt
   return linear_dx(a, (cudaStream_t)stream);
 }
 
+int rq_merge_lora(int wfmt, const void* qweight, const void* scales, int scale_dtype, const uint8_t* c2,
+                  const float* c2_scales, int64_t N, int64_t K, int block_size, const float* lora_a,
+                  const float* lora_b, int r, float scaling, int mode, void* out, int out_dtype, void* stream) {
+  RQ_PROLOGUE();
+  int rc = check_weight(wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size);
+  if (rc != RQ_OK) return rc;
+  if (!dtype_ok(out_dtype)) return RQ_ERR_DTYPE;
+  if (r < 0 || r > 128 || (r > 0 && (!lora_a || !lora_b)) || (N * K > 0 && !out)) return RQ_ERR_INVALID;
+  if (mode != RQ_MERGE_FP32_SUM && mode != RQ_MERGE_ROUND_EACH) return RQ_ERR_INVALID;
+  if ((uintptr_t)out % dtype_size(out_dtype)) return RQ_ERR_ALIGN;
+  const QWeight w{wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size};
+  return merge_weight(w, lora_a, lora_b, r, scaling, mode, out, out_dtype, (cudaStream_t)stream);
+}
+
 void launch_int4_dequant_matmul(void* stream, void* x, void* w_packed, void* scales, void* c, int M, int N, int K,
                                 int block_size) {
   g_last_status = rq_linear_forward(RQ_W_NF4, w_packed, scales, RQ_F16, nullptr, nullptr, N, K, block_size, x,

@@ -92,6 +92,8 @@ bool gemv_supported(const LinearArgs& a);
 int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st);
 
 int linear_forward(const LinearArgs& a, cudaStream_t st);
+int merge_weight(const QWeight& w, const float* A, const float* B, int r, float s, int mode, void* out, int odt,
+                 cudaStream_t st);
 int linear_dx(const LinearArgs& a, cudaStream_t st);
 int64_t linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int r);
 

@@ -60,12 +60,19 @@ class LoRALinear(nn.Module):
 
     def merge_lora(self) -> None:
         """Store W + B @ A * scaling as an fp16 weight (no re-quantization)
-        and zero the adapters; unmerge_lora() reverts."""
+        and zero the adapters; unmerge_lora() reverts.  On the GPU the merged
+        weight comes from one kernel pass over the codes (rq_merge_lora)."""
         if self.merged:
             raise RuntimeError("LoRA already merged")
-        delta_W = (self.lora_B @ self.lora_A) * self.scaling
-        base_weight_fp = self.base_layer.dequantized_weight()
-        merged_weight = (base_weight_fp + delta_W.to(base_weight_fp.dtype)).to(torch.float16)
+        b = self.base_layer
+        if isinstance(b, QuantLinear) and b.weight_quant.is_cuda:
+            # dequantize, B @ A * scaling and the fp32 add in one pass over the codes
+            merged_weight = layer_ops.merge_weight(b.weight_view(), self.lora_A, self.lora_B, self.scaling,
+                                                   layer_ops.MERGE_FP32_SUM, torch.float16)
+        else:
+            delta_W = (self.lora_B @ self.lora_A) * self.scaling
+            base_weight_fp = b.dequantized_weight()
+            merged_weight = (base_weight_fp + delta_W.to(base_weight_fp.dtype)).to(torch.float16)
         self.base_layer.merged_fp16_weight = merged_weight
         self.base_layer.merged_mode = True
         self.merged = True

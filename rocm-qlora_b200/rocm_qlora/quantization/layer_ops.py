@@ -277,3 +277,24 @@ class LoRAQuantFunction(torch.autograd.Function):
             if need_xd and ctx.has_xd:
                 gxd = (gt @ A).view(ctx.x_shape)
         return gx, gA, gB, gxd, None, None, None
+
+
+MERGE_FP32_SUM, MERGE_ROUND_EACH = 0, 1
+
+
+def merge_weight(w: WeightView, A: Optional[torch.Tensor], B: Optional[torch.Tensor], scaling: float, mode: int,
+                 out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """[N, K] weight deq(W) + scaling * B @ A in one kernel pass (rq_merge_lora):
+    mode MERGE_FP32_SUM adds in fp32 and rounds once (merge_lora),
+    MERGE_ROUND_EACH rounds both terms to out_dtype before adding
+    (_export_dequant_layer).  A [r, K] and B [N, r] are used as fp32."""
+    L = nat.lib()
+    dev = w.device
+    r = 0 if A is None else A.shape[0]
+    out = torch.empty(w.N, w.K, dtype=out_dtype, device=dev)
+    with torch.cuda.device(dev):
+        A32 = A.detach().to(device=dev, dtype=torch.float32).contiguous() if r else None
+        B32 = B.detach().to(device=dev, dtype=torch.float32).contiguous() if r else None
+        nat.check(L.rq_merge_lora(*w.args(), nat.ptr(A32), nat.ptr(B32), r, float(scaling), mode, out.data_ptr(),
+                                  nat.dtype_code(out_dtype), nat.stream_ptr(dev)), "rq_merge_lora")
+    return out

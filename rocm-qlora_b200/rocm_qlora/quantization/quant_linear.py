@@ -102,6 +102,33 @@ class QuantLinear(nn.Module):
             w = dequantize_int4(self.weight_quant, self.weight_scales, block_size=self.block_size)
         return w.reshape(-1)[:n].reshape(self.original_shape)
 
+    _QUANT_BUFFERS = ("weight_quant", "weight_scales", "c2", "c2_scales")
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        """Loads quantized buffers whatever this module held before: a layer
+        built unquantized (empty buffers) or quantized with another shape
+        takes the checkpoint's shapes and dtypes, and a checkpoint carrying
+        double-quantized scales (c2, c2_scales) switches the layer to them,
+        so a state dict written by the reference loads into a fresh layer."""
+        dq_keys = [prefix + k in state_dict for k in ("c2", "c2_scales")]
+        if all(dq_keys):
+            c2 = state_dict[prefix + "c2"]
+            for k in ("c2", "c2_scales"):
+                if k not in self._buffers:
+                    self.register_buffer(k, torch.empty(0, device=self.weight_quant.device))
+            self.use_double_quant = True
+            self.use_fp8_c2 = c2.dtype != torch.int8
+            self.blocksize_2 = getattr(self, "blocksize_2", 256)
+        for k in self._QUANT_BUFFERS:
+            t = state_dict.get(prefix + k)
+            cur = self._buffers.get(k)
+            if isinstance(t, torch.Tensor) and isinstance(cur, torch.Tensor) and (
+                    cur.shape != t.shape or cur.dtype != t.dtype):
+                self._buffers[k] = torch.empty(t.shape, dtype=t.dtype, device=cur.device)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+
     def weight_view(self) -> layer_ops.WeightView:
         """The C ABI's view of the quantized buffers, rebuilt only when a
         buffer was replaced (module moves, new tensors) or written in place

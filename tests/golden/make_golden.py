@@ -2,7 +2,9 @@
 
 Usage (in a container where the reference checkout is present):
 
-    python tests/golden/make_golden.py /path/to/ROCM-QLORA
+    python tests/golden/make_golden.py /path/to/ROCM-QLORA [state_dicts]
+
+(the optional second argument writes only state_dicts.npz).
 
 The reference package ``rocm_qlora`` is pure Python on torch.  Its ``.py``
 sources are copied into a temporary directory (so no shipped bytecode is
@@ -59,16 +61,56 @@ def sha(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
-def main(ref_path: str) -> None:
+def main(ref_path: str, only: str = "") -> None:
     os.environ["ROCM_QLORA_QUIET"] = "1"
     sys.dont_write_bytecode = True
     tmp = tempfile.mkdtemp(prefix="rq_ref_")
     try:
         _copy_reference(ref_path, tmp)
         sys.path.insert(0, tmp)
-        run(tmp)
+        if only == "state_dicts":
+            run_state_dicts()
+        else:
+            run(tmp)
+            run_state_dicts()
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
+
+
+def run_state_dicts() -> None:
+    """state_dicts.npz: LoRALinear(QuantLinear) state dicts written by the
+    reference (every tensor's bits and dtype under its state_dict key) with
+    an input and the reference's eval-mode output, so that loading a
+    reference checkpoint into this package can be checked."""
+    import torch.nn as nn
+    from rocm_qlora.quantization.quant_linear import QuantLinear
+    from rocm_qlora.lora.lora_layer import LoRALinear
+    out = {}
+    for name, N, K, M, bits_, bias, dq_ in (("nf4_bias", 192, 512, 4, 4, True, False),
+                                           ("nf4dq", 256, 1024, 8, 4, False, True),
+                                           ("int8", 160, 512, 3, 8, True, False)):
+        inp = layer_inputs(N, K, M, sigma=0.05, r=8, alpha=16, seed=N + K)
+        lin = nn.Linear(K, N, bias=bias).to(torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_(inp.W)
+            if bias:
+                lin.bias.copy_((torch.randn(N, generator=torch.Generator().manual_seed(N)) * 0.1).to(torch.bfloat16))
+        ql = QuantLinear.from_linear(lin, bits=bits_, block_size=64)
+        if dq_:
+            ql.enable_double_quant()
+        lora = LoRALinear(ql, r=8, lora_alpha=16, lora_dropout=0.0).eval()
+        with torch.no_grad():
+            lora.lora_A.copy_(inp.A)
+            lora.lora_B.copy_(inp.B)
+            y = lora(inp.X)
+        for k, t in lora.state_dict().items():
+            out[f"{name}/sd/{k}"] = bits(t)
+            out[f"{name}/dtype/{k}"] = np.array(str(t.dtype).replace("torch.", ""))
+        out[f"{name}/meta"] = np.array([N, K, M, bits_, int(bias), int(dq_)])
+        out[f"{name}/x"], out[f"{name}/y"] = bits(inp.X), bits(y)
+    out["torch"] = np.array(torch.__version__)
+    np.savez_compressed(os.path.join(HERE, "state_dicts.npz"), **out)
+    print("wrote state_dicts.npz with torch", torch.__version__)
 
 
 def run(tmp: str) -> None:
@@ -266,6 +308,6 @@ def run(tmp: str) -> None:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <path to the ROCM-QLORA checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: make_golden.py <path to the ROCM-QLORA checkout> [state_dicts]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) == 3 else "")

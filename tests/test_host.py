@@ -164,3 +164,31 @@ def test_weight_view_cache_follows_buffers():
     with torch.inference_mode():
         qi = QuantLinear(256, 128, bits=4)
     assert qi.weight_view() is not qi.weight_view()
+
+
+def test_export_helpers_host_side():
+    """The export module's host-only helpers (size estimate, conversion
+    steps) -- the reference's gguf_export.py API."""
+    from rocm_qlora.export import estimate_gguf_size, get_gguf_conversion_instructions
+    e = estimate_gguf_size(7_000_000_000, "q4_k_m")
+    assert e["bits_per_param"] == 4.5 and e["quant_type"] == "q4_k_m"
+    assert abs(e["estimated_size_gb"] - 7e9 * 4.5 / 8 / 1e9 * 1.05) < 0.01
+    assert estimate_gguf_size(10, "nope")["bits_per_param"] == 4.5
+    text = get_gguf_conversion_instructions("/tmp/m.safetensors")
+    assert "convert_hf_to_gguf.py /tmp/m.safetensors" in text and "q4_k_m" in text
+
+
+def test_cast_param_cache():
+    """Adapter casts are reused while the parameter is unchanged and redone
+    after an in-place update or forget_casts()."""
+    from rocm_qlora.quantization import layer_ops as lo
+    p = torch.nn.Parameter(torch.randn(4, 8))
+    a = lo.cast_param(p, torch.bfloat16)
+    assert lo.cast_param(p, torch.bfloat16) is a
+    with torch.no_grad():
+        p.add_(1)
+    c = lo.cast_param(p, torch.bfloat16)
+    assert c is not a and torch.equal(c, p.detach().bfloat16())
+    p.data.zero_()  # not seen by the version counter ...
+    lo.forget_casts(p)  # ... hence the explicit reset
+    assert float(lo.cast_param(p, torch.bfloat16).abs().sum()) == 0
