@@ -328,6 +328,8 @@ def run_ours(args, rank, world, device):
     # configs[2] (prefill / training GEMM), single GPU
     prefill = prefill_leg(device) if (world == 1 and not args.no_prefill) else None
     c5 = c5_leg(device) if (world == 1 and not args.no_prefill) else None
+    if world > 1 and not args.no_prefill:
+        c5 = c5_sharded_leg(device, rank, world)
     quant = quant_leg(device, no_cpu=args.no_cpu) if (world == 1 and not args.no_prefill) else None
     c4 = c4_leg(device) if (world == 1 and not args.no_prefill and not args.no_model) else None
 
@@ -661,6 +663,130 @@ def c4_leg(device, steps=4, warmup=2, batch=4, seq=2048):
     del model, opt, params, ids
     torch.cuda.empty_cache()
     return out
+
+
+def c5_sharded_leg(device, rank, world, iters=20):
+    """configs[4] across the node (strong scaling): each 70B-shaped layer
+    W[N, K] in {8192x28672, 28672x8192}, NF4 + double quant, LoRA r16 a32,
+    built whole on every rank (same seed) and column-sharded without
+    re-quantizing (ColumnParallelLinear.from_quant_linear: N/p rows a rank).
+    Decode M in {1, 16} gathers Y inside the GEMV (fused, NVLink stores);
+    prefill M = 4096 runs the tensor-core GEMM on the shard and an NCCL
+    all-gather of Y, whose time is reported on its own.  Per call: the max
+    over ranks of the CUDA-event time (graph replays for decode, eager calls
+    for prefill), and the same layer unsharded on rank 0 alone (t1), so that
+    efficiency = t1 / (p * tp)."""
+    import torch.distributed as dist
+    import torch.nn as nn
+    from rocm_qlora import LoRALinear, QuantLinear
+    from rocm_qlora.distributed import ColumnParallelLinear
+
+    def tmax(ms):
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def event_time(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize(device)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / n
+
+    out = {}
+    for (N, K) in C5_SHAPES:
+        g = torch.Generator(device=device).manual_seed(N)
+        W = (torch.randn(N, K, generator=g, device=device) * 0.015).to(torch.bfloat16)
+        lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=device)
+        with torch.no_grad():
+            lin.weight.copy_(W)
+        del W
+        ql = QuantLinear.from_linear(lin, bits=4)
+        ql.enable_double_quant()
+        full = LoRALinear(ql, r=16, lora_alpha=32).to(device).eval()
+        with torch.no_grad():
+            full.lora_A.copy_((torch.rand(16, K, generator=g, device=device) * 2 - 1) / K ** 0.5)
+            full.lora_B.copy_(torch.randn(N, 16, generator=g, device=device) * 0.01)
+        del lin
+        cp = ColumnParallelLinear.from_quant_linear(full, gather_tokens=16).eval()
+        wbytes = N * K // 2 + N * K // 64 + 4 * (N * K // 64 // 256 + 1)
+        for M in (1, 16, 4096):
+            x = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16)
+            with torch.no_grad():
+                if M <= 16:  # fused gather, graph-replayed
+                    s = torch.cuda.Stream(device)
+                    s.wait_stream(torch.cuda.current_stream(device))
+                    with torch.cuda.stream(s):
+                        for _ in range(3):
+                            cp(x)
+                    torch.cuda.current_stream(device).wait_stream(s)
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr):
+                        cp(x)
+                    tp = tmax(event_time(gr.replay, iters))
+                    del gr
+                    coll = None
+                else:  # GEMM on the shard + NCCL all-gather of Y
+                    for _ in range(2):
+                        cp(x)
+                    tp = tmax(event_time(lambda: cp(x), 5))
+                    y_loc = cp.local(x)
+                    buf = torch.empty(world * M, max(cp.sizes), dtype=y_loc.dtype, device=device)
+                    yl = torch.nn.functional.pad(y_loc, (0, max(cp.sizes) - y_loc.shape[1])).contiguous()
+                    coll = tmax(event_time(lambda: dist.all_gather_into_tensor(buf, yl), 5))
+                t1 = torch.zeros(1, device=device, dtype=torch.float64)
+                if rank == 0:  # the unsharded layer alone
+                    if M <= 16:
+                        s = torch.cuda.Stream(device)
+                        s.wait_stream(torch.cuda.current_stream(device))
+                        with torch.cuda.stream(s):
+                            for _ in range(3):
+                                full(x)
+                        torch.cuda.current_stream(device).wait_stream(s)
+                        gr = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(gr):
+                            full(x)
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        torch.cuda.synchronize(device)
+                        e0.record()
+                        for _ in range(iters):
+                            gr.replay()
+                        e1.record()
+                        torch.cuda.synchronize(device)
+                        t1[0] = e0.elapsed_time(e1) / iters
+                        del gr
+                    else:
+                        for _ in range(2):
+                            full(x)
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        torch.cuda.synchronize(device)
+                        e0.record()
+                        for _ in range(5):
+                            full(x)
+                        e1.record()
+                        torch.cuda.synchronize(device)
+                        t1[0] = e0.elapsed_time(e1) / 5
+                dist.broadcast(t1, src=0)
+            t1 = float(t1.item())
+            rec = {"us": round(tp * 1e3, 2), "us_1gpu": round(t1 * 1e3, 2),
+                   "efficiency": round(t1 / (world * tp), 4)}
+            if M <= 16:
+                rec["GB/s"] = round((wbytes + 2 * M * (K + N)) / (tp * 1e-3) / 1e9, 1)
+            else:
+                rec["TFLOP/s"] = round(2.0 * M * N * K / (tp * 1e-3) / 1e12, 1)
+                rec["allgather_us"] = round(coll * 1e3, 2)
+            out[f"{N}x{K}/M{M}"] = rec
+            del x
+        cp.close()
+        del cp, full, ql
+        torch.cuda.empty_cache()
+    return {"config": f"configs[4]: 70B-shaped NF4+DQ layers, LoRA r16 a32, column-sharded over {world} GPUs "
+                      "(strong scaling; decode gathers Y in the GEMV, prefill with an NCCL all-gather)",
+            "calls": out}
 
 
 def rotated_modules(layers, wsets):
