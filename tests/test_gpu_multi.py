@@ -233,6 +233,50 @@ def _worker_missing_rank(rank: int, world: int, port: int, q) -> None:
             dist.destroy_process_group()
 
 
+def _worker_prequantized(rank: int, world: int, port: int, q) -> None:
+    """A layer quantized whole (as a checkpoint holds it) and sharded with
+    ColumnParallelLinear.from_quant_linear: the fused decode output equals
+    the unsharded layer's bit for bit, also when K = 11008 puts second-level
+    groups across rows (shards start at multiples of 64 rows)."""
+    import torch.distributed as dist
+    import torch.nn as nn
+    from rocm_qlora import LoRALinear, QuantLinear
+    from rocm_qlora.distributed import ColumnParallelLinear
+    ok = False
+    try:
+        dev = _setup(rank, world, port)
+        msgs = []
+        for (N, K, M) in ((2048, 11008, 16), (1000, 4096, 1)):
+            g = torch.Generator().manual_seed(N + K)
+            lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=dev)
+            with torch.no_grad():
+                lin.weight.copy_((torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(dev))
+            ql = QuantLinear.from_linear(lin, bits=4)
+            ql.enable_double_quant()
+            full = LoRALinear(ql, r=16, lora_alpha=32).to(dev).eval()
+            with torch.no_grad():
+                full.lora_A.copy_(((torch.rand(16, K, generator=g) * 2 - 1) / K ** 0.5).to(dev))
+                full.lora_B.copy_((torch.randn(N, 16, generator=g) * 0.01).to(dev))
+            cp = ColumnParallelLinear.from_quant_linear(full, gather_tokens=16).eval()
+            x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+            with torch.no_grad():
+                y = cp(x).clone()
+                y_full = full(x)
+            assert not cp.peer.error()
+            assert torch.equal(y, y_full), f"sharded != unsharded for {(N, K, M)}"
+            cp.close()
+            msgs.append(f"{(N, K, M)} ok")
+        ok = True
+        q.put((rank, "ok", msgs))
+    except Exception as e:
+        q.put((rank, repr(e), []))
+    finally:
+        if dist.is_initialized():
+            if ok:
+                dist.barrier()
+            dist.destroy_process_group()
+
+
 def _run_two(target, n_msgs):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -268,3 +312,8 @@ def test_fused_gather_slow_reader():
 @TWO_GPUS
 def test_fused_gather_missing_rank_times_out():
     _run_two(_worker_missing_rank, 1)
+
+
+@TWO_GPUS
+def test_prequantized_layer_sharded_two_ranks():
+    _run_two(_worker_prequantized, 2)
