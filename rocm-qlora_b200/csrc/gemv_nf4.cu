@@ -89,42 +89,53 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// The end of a gathering call, run by one thread of every CTA after a CTA
-// barrier has ordered the CTA's stores before it.  Each CTA arrives with an
+// The end of a gathering call, run by one warp of every CTA after a CTA
+// barrier has ordered the CTA's stores before it.  Lane 0 arrives with an
 // acquire-release atomic (GPU scope); the last CTA to arrive has thereby
-// acquired every CTA's stores.  It advances the epoch and publishes it in
-// every rank's flag slot for this rank with a release at system scope
-// (cumulative: the rank's stores to all ranks' Y are visible before the
-// flag), then waits, at most about 2 s, until every rank's flag here holds
-// the epoch (acquire at system scope): from then on every rank's shard of
-// this call is in this rank's Y.  One system-scope release per call is the
-// whole fence cost (a system fence in every CTA cost ~5 us a call).  The
-// arrival counter goes back to zero for the next call.
-__device__ void gather_arrive(const RqGather& g) {
+// acquired every CTA's stores.  Its warp advances the epoch and publishes it
+// to every rank at once, lane q to rank q's flag slot for this rank: each
+// lane fences at system scope (cumulative, after the warp barrier that
+// follows lane 0's acquire: every CTA's stores to all ranks' Y become
+// visible before the flag) and stores the flag relaxed.  Lane q then waits,
+// at most about 2 s, until rank q's flag here holds the epoch (acquire at
+// system scope): from then on every rank's shard of this call is in this
+// rank's Y.  The arrival counter goes back to zero for the next call.
+__device__ void gather_arrive(const RqGather& g, int lane) {
   uint32_t* ctrl = g.ctrl;
-  uint32_t arrived;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(ctrl) : "memory");
+  uint32_t arrived = 0;
+  if (lane == 0)
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(ctrl) : "memory");
+  arrived = __shfl_sync(0xffffffffu, arrived, 0);
   if (arrived != gridDim.x - 1) return;
-  ctrl[0] = 0;
-  const uint32_t epoch = ctrl[1] + 1;
-  ctrl[1] = epoch;
-  for (int q = 0; q < g.world; ++q) {
+  const uint32_t epoch = *reinterpret_cast<volatile const uint32_t*>(ctrl + 1) + 1;
+  __syncwarp();
+  if (lane == 0) {
+    ctrl[0] = 0;
+    ctrl[1] = epoch;
+  }
+  for (int q = lane; q < g.world; q += 32) {
     uint32_t* f = g.flags[q] + g.rank;
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
   }
   const uint64_t t0 = global_ns();
-  for (int q = 0; q < g.world; ++q) {
+  bool ok = true;
+  for (int q = lane; q < g.world; q += 32) {
     for (;;) {
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.my_flags + q) : "memory");
       if ((int32_t)(v - epoch) >= 0) break;
       if (global_ns() - t0 > 2000000000ull) {
-        ctrl[2] = 1;
-        atomicAdd(&g_kernel_timeouts, 1u);
-        return;
+        ok = false;
+        break;
       }
-      __nanosleep(64);
+      __nanosleep(32);
     }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && lane == 0) {
+    ctrl[2] = 1;
+    atomicAdd(&g_kernel_timeouts, 1u);
   }
 }
 
@@ -132,15 +143,18 @@ __device__ void gather_arrive(const RqGather& g) {
 // its end) is the control block's epoch + 1; every CTA reads it at its
 // start, before any CTA can have arrived, so all CTAs read the same value.
 // CTA 0 announces to every rank that this rank has entered the call (its
-// stream has passed every earlier consumer of its Y).
-__device__ uint32_t gather_enter(const RqGather& g) {
-  const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(g.ctrl + 1) + 1;
-  if (blockIdx.x == 0)
-    for (int q = 0; q < g.world; ++q) {
-      uint32_t* f = g.flags[q] + g.world + g.rank;
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-    }
-  return e;
+// stream has passed every earlier consumer of its Y), lane q to rank q.
+// The announcement orders nothing (every earlier kernel of this stream has
+// finished), so the stores are relaxed: no fence on the kernel's start.
+__device__ uint32_t gather_epoch_of(const RqGather& g) {
+  return *reinterpret_cast<volatile const uint32_t*>(g.ctrl + 1) + 1;
+}
+__device__ void gather_enter(const RqGather& g, uint32_t epoch, int lane) {
+  if (blockIdx.x != 0) return;
+  for (int q = lane; q < g.world; q += 32) {
+    uint32_t* f = g.flags[q] + g.world + g.rank;
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+  }
 }
 
 // Before a CTA stores its outputs into the other ranks' Y: wait (at most
@@ -480,6 +494,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   }
 
   // ---- consumers
+  if (p.gather && warp == 0) {  // announce this rank's entry first thing
+    const uint32_t e = gather_epoch_of(p.gth);
+    gather_enter(p.gth, e, lane);
+    if (lane == 0) gather_epoch = e, gather_skip = 0;
+  }
   unsigned char* lut = smem;
   float* sc = reinterpret_cast<float*>(smem + q.sc_off);
   float* sclut = reinterpret_cast<float*>(smem + q.aux_off);
@@ -585,10 +604,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   }
   if (fmt != RQ_W_NF4 && tid < 256)
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
-  if (p.gather && tid == 0) {
-    gather_epoch = gather_enter(p.gth);
-    gather_skip = 0;
-  }
 
   start_wait();  // the producer's mbarriers and flags are initialized
   uint32_t u = 0;       // stages consumed (over all passes)
@@ -794,7 +809,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // every consumer's stores of the call are ordered before the arrival by
     // the barrier; the arrival's release covers them
     consumer_sync();
-    if (tid == 0) gather_arrive(p.gth);
+    if (warp == 0) gather_arrive(p.gth, lane);
   }
 }
 
