@@ -313,6 +313,10 @@ def run_ours(args, rank, world, device):
         except Exception:
             traffic = None
 
+    # this library's kernels in one step (counted by the profiler, outside
+    # the timed region)
+    launches_per_step = count_rq_kernels(lambda: run_steps(1, 0, True, graphs), device)
+
     # graphs that hold NCCL calls are released before the process group goes
     del graphs, gemv_graphs
     torch.cuda.synchronize(device)
@@ -353,7 +357,7 @@ def run_ours(args, rank, world, device):
                          "launches": n_launch, "us_per_launch": round(ms_g * 1e3 / n_launch, 3)},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps * len(calls) * 2,
+            "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks,
             "prefill": prefill,
             "c5": c5,
@@ -789,6 +793,17 @@ def c5_sharded_leg(device, rank, world, iters=20):
             "calls": out}
 
 
+def count_rq_kernels(fn, device):
+    """Kernels of this library (namespace rq) that one call of fn launches."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize(device)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize(device)
+    return sum(1 for e in prof.events()
+               if e.device_type == torch.autograd.DeviceType.CUDA and "rq::" in e.name)
+
+
 def rotated_modules(layers, wsets):
     """LoRALinear modules sharing the adapters of `layers` but reading the
     rotated weight copies, so the public-API leg streams from HBM too."""
@@ -811,20 +826,31 @@ def rotated_modules(layers, wsets):
 
 
 def run_e2e(args, mods, device, world):
-    """Public-API timing: pinned host X -> device, LoRALinear.forward, Y -> host."""
+    """Public-API timing: pinned host X -> device, LoRALinear.forward, Y -> host.
+
+    A step's nine inputs sit in one pinned host buffer and go to the device
+    in one copy; its nine outputs are gathered into one device buffer and
+    come back in one copy (one H2D and one D2H transfer a step)."""
     g = torch.Generator().manual_seed(9)
-    hx = {(si, M): torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory()
-          for si, (N, K) in enumerate(SHAPES) for M in MS}
-    hy = {(si, M): torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-          for si, (N, K) in enumerate(SHAPES) for M in MS}
     calls = [(si, M) for si in range(len(SHAPES)) for M in MS]
+    xo, yo, off_x, off_y = {}, {}, 0, 0
+    for si, M in calls:
+        N, K = SHAPES[si]
+        xo[(si, M)], yo[(si, M)] = off_x, off_y
+        off_x += M * K
+        off_y += M * N
+    hx_all = torch.randn(off_x, generator=g).to(torch.bfloat16).pin_memory()
+    hy_all = torch.empty(off_y, dtype=torch.bfloat16).pin_memory()
+    xd_all = torch.empty(off_x, dtype=torch.bfloat16, device=device)
+    yd_all = torch.empty(off_y, dtype=torch.bfloat16, device=device)
+    xv = {(si, M): xd_all[xo[(si, M)]:xo[(si, M)] + M * SHAPES[si][1]].view(M, SHAPES[si][1]) for si, M in calls}
 
     def one(c):
         with torch.no_grad():
-            for si, M in calls:
-                x = hx[(si, M)].to(device, non_blocking=True)
-                y = mods[c % len(mods)][si](x)
-                hy[(si, M)].copy_(y, non_blocking=True)
+            xd_all.copy_(hx_all, non_blocking=True)
+            ys = [mods[c % len(mods)][si](xv[(si, M)]).view(-1) for si, M in calls]
+            torch.cat(ys, out=yd_all)
+            hy_all.copy_(yd_all, non_blocking=True)
 
     for i in range(max(3, args.warmup)):
         one(i)
@@ -844,27 +870,22 @@ def run_e2e(args, mods, device, world):
     d2h = sum(M * SHAPES[si][0] * 2 for si, M in calls)
     eager = step_bytes * args.steps * world / dt / 1e9
 
-    # The same public calls captured once per weight copy in a CUDA graph,
-    # each step still copying its inputs from pinned host memory and its
-    # outputs back (a decode loop's usual form): replayed and wall-clocked.
-    xd = {k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in hx.items()}
+    # The same step captured once per weight copy in a CUDA graph, each step
+    # still copying its inputs from pinned host memory and its outputs back
+    # (a decode loop's usual form): replayed and wall-clocked.
     graphs = []
     with torch.no_grad():
         s = torch.cuda.Stream(device)
         s.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(s):
             for c in range(len(mods)):
-                for si, M in calls:
-                    mods[c][si](xd[(si, M)])
+                one(c)
         torch.cuda.current_stream(device).wait_stream(s)
         torch.cuda.synchronize(device)
         for c in range(len(mods)):
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
-                for si, M in calls:
-                    xd[(si, M)].copy_(hx[(si, M)], non_blocking=True)
-                    y = mods[c][si](xd[(si, M)])
-                    hy[(si, M)].copy_(y, non_blocking=True)
+                one(c)
             graphs.append(gr)
     for i in range(max(3, args.warmup)):
         graphs[i % len(graphs)].replay()
@@ -883,9 +904,10 @@ def run_e2e(args, mods, device, world):
     return {"value": round(step_bytes * args.steps * world / dtg / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "eager_value": round(eager, 2),
-            "note": "LoRALinear.forward (each rank its shard) on pinned host inputs: every step copies X in and "
-                    "Y out; value = the calls captured in CUDA graphs and replayed, eager_value = plain Python "
-                    "calls; wall clock, max over ranks"}
+            "note": "LoRALinear.forward (each rank its shard) on pinned host inputs: every step copies the nine "
+                    "calls' X in (one H2D copy from a pinned buffer) and their Y out (gathered on the device, one "
+                    "D2H copy); value = the step captured in CUDA graphs and replayed, eager_value = plain "
+                    "Python calls; wall clock, max over ranks"}
 
 
 # --------------------------------------------------------- CPU reference
@@ -960,6 +982,29 @@ def run_case(args, device):
     from rocm_qlora import LoRALinear, QuantLinear
     from tests.inputs import layer_inputs
     parts = args.case.split(":")
+    if parts[0] == "quant":  # quant:N:K -- rq_nf4_quantize of a bf16 [N, K] weight, repeated
+        from rocm_qlora import _native as nat
+        N, K = int(parts[1]), int(parts[2])
+        L = nat.lib()
+        W = (torch.randn(N, K, device=device) * 0.02).to(torch.bfloat16)
+        packed = torch.empty(N * K // 2, dtype=torch.uint8, device=device)
+        sc = torch.empty(N * K // 64, dtype=torch.bfloat16, device=device)
+        st = torch.cuda.current_stream(device).cuda_stream
+        fn = lambda: L.rq_nf4_quantize(W.data_ptr(), nat.BF16, N * K, 64, packed.data_ptr(), sc.data_ptr(), st)  # noqa: E731
+        for _ in range(3):
+            assert fn() == 0
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        n = N * K
+        print(json.dumps({"case": args.case, "us_per_call": round(us, 3),
+                          "gbs": round((2 * n + n // 2 + 2 * n // 64) / us / 1e3, 1)}))
+        return
     kind, N, K, M = parts[0], int(parts[1]), int(parts[2]), int(parts[3])
     r = int(parts[4]) if len(parts) > 4 else R
     inp = layer_inputs(N, K, M, sigma=0.02, r=max(r, 1), alpha=2 * max(r, 1), seed=1, with_dy=kind == "dx")

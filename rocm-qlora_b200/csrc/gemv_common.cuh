@@ -52,7 +52,16 @@ struct GemvArgs {
   int xdt;             // activation dtype (RQ_BF16 / RQ_F16)
   int gather;          // nonzero: output into every rank's Y per gth (NF4 kernel only)
   RqGather gth;
+  // LoRA down product fused into the NF4 GEMV's grid (fuse_down != 0): the
+  // grid's first kNfDownCtas CTAs write the partial sums of lora_x . lora_a^T
+  int fuse_down;
+  const void* lora_x;  // [M, K]
+  const void* lora_a;  // [r, K]
+  float* partial;      // [kNfDownCtas][M][r] fp32 (workspace)
+  unsigned* counters;  // workspace counter area: [0] down CTAs done, [2] GEMV CTAs done
 };
+
+constexpr int kNfDownCtas = 8;  // CTAs of the fused down product
 
 // mma.sync m16n8k16 with a zero accumulator input (starts a block partial)
 template <int DT> struct Mma16816Zero;
@@ -105,12 +114,13 @@ inline int num_sms() {
 constexpr size_t kGemvSmemCap = 113 * 1024;  // two CTAs per SM
 
 // NF4-family GEMV (gemv_nf4.cu): whether a shape fits its shared memory, and
-// the launch (grid and tiling chosen inside; `pdl`: launched as the
-// programmatic dependent of the LoRA down-product kernel).
+// the launch (grid and tiling chosen inside; always a programmatic launch;
+// `beside`: the LoRA down-product kernel runs beside it, so the grid leaves
+// that kernel's SMs free).
 bool gemv_nf4_fits(const QWeight& w, int64_t M, int r);
 // decode numerics (rq_set_decode_exact)
 bool decode_exact();
 void set_decode_exact(int on);
-int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st);
+int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st);
 
 }  // namespace rq

@@ -301,6 +301,15 @@ static void gemv_shape(int wk, int64_t N, int64_t K, int64_t M, int r, int* grid
   *nt = (int)n;
 }
 
+// Whether the NF4 GEMV can compute the layer's LoRA down product in its own
+// grid (gemv_nf4.cu, down_role): an adapter of rank <= 64, no fused gather,
+// 4-byte aligned x_lora rows and A rows (K is a multiple of 64).
+bool gemv_fuse_down(const LinearArgs& a) {
+  return is_nf4_fmt(a.w.fmt) && a.r > 0 && a.r <= 64 && a.M >= 1 && a.M <= 16 && a.gather == nullptr &&
+         a.lora_x != nullptr && a.lora_a != nullptr && ((uintptr_t)a.lora_x % 4) == 0 &&
+         ((uintptr_t)a.lora_a % 4) == 0;
+}
+
 bool gemv_supported(const LinearArgs& a) {
   if (a.M < 1 || a.M > 16) return false;
   if (a.xdt != RQ_BF16 && a.xdt != RQ_F16) return false;
@@ -348,7 +357,7 @@ static int gemv_dt(const GemvArgs& g, int wk, int nt, size_t smem, cudaStream_t 
   return m16 ? gemv_nt<DT, 2, 16>(g, nt, smem, st) : gemv_nt<DT, 2, 8>(g, nt, smem, st);
 }
 
-int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
+int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st, float* partial, unsigned* counters) {
   GemvArgs g;
   g.w = a.w;
   g.x = a.x;
@@ -363,6 +372,12 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st) {
   g.xdt = a.xdt;
   g.gather = a.gather != nullptr;
   if (a.gather) g.gth = *a.gather;
+  // with `partial` the NF4 GEMV computes tdown itself (gemv_fuse_down)
+  g.fuse_down = partial != nullptr;
+  g.lora_x = a.lora_x;
+  g.lora_a = a.lora_a;
+  g.partial = partial;
+  g.counters = counters;
   if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_forward(g, a.r > 0, st);
   if (a.gather) return RQ_ERR_UNSUPPORTED;  // the INT8 kernel has no gather epilogue
   const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;

@@ -38,16 +38,21 @@
 //    consumers decode them (fp8/int8 second level times c2_scales) into
 //    fragment order; the scale multiplies each block's fp32 partial.
 //
-// With LoRA the layer's down product x.A^T comes from the kernel launched
-// just before this one.  This kernel is then launched as its programmatic
-// dependent: it streams the weights while the down product runs and waits
-// for it (griddepcontrol.wait) only before the epilogue reads x.A^T.  Every
-// other input was written by kernels that had finished before the
-// down-product kernel let this one launch: the down product is itself a
-// programmatic dependent of the kernel before it and triggers this kernel
-// only after its own griddepcontrol.wait.  This kernel triggers at its
-// start, so the next layer's down product can be resident (waiting) while
-// it runs.
+// Launch chain: this kernel is always launched as the programmatic dependent
+// of the kernel before it in the stream, and triggers its own dependent at
+// its start.  A CTA therefore starts as soon as an SM is free -- typically
+// the moment the previous layer's CTA there exits -- and streams what no
+// kernel of the chain writes (codes, scales, c2 / c2_scales, LoRA B) into
+// its ring straight away.  Everything another kernel may still be writing
+// is read after griddepcontrol.wait, which returns once the grid before
+// this one has finished and its writes are visible: X (without an adapter
+// the producer waits after the first ring fill of codes, then issues X for
+// those stages), x.A^T and the bias (the epilogue), and with the fused
+// gather the flags and counters of the calls before (the whole kernel
+// waits first).  With LoRA the grid before is the layer's down-product
+// kernel; it lets this one launch only after its own griddepcontrol.wait,
+// so X is complete at launch and is streamed with the codes from the first
+// stage, while the down product runs beside the main loop.
 //
 // All waits are bounded: a wait that runs out raises the CTA's abort flag,
 // the CTA lets its issued copies land (bounded) and returns without writing
@@ -196,6 +201,9 @@ struct Nf4Args {
   int sp;            // floats per block row of the staged scales (NT * 16 + 2)
   int esz;           // bytes per raw scale (1: c2 codes; 2/4: plain scales)
   int wide;          // 1: 3-D code box (K % 256 == 0)
+  int xsafe;         // 1: X is complete when this grid launches (it follows the
+                     // down-product kernel, which lets it launch only after
+                     // its own griddepcontrol.wait), so X is loaded at once
   int slots;         // ring stages S
   uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X), a multiple of 1024
   uint32_t ring_off;    // dynamic offsets: ring (rounded up to 1024 in the shared window),
@@ -284,6 +292,123 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   atomicAdd(&g_kernel_timeouts, 1u);
   return false;
 }
+
+// ---- LoRA down product fused into the grid (GemvArgs::fuse_down)
+//
+// The grid's first kNfDownCtas CTAs compute the partial sums of
+// t = x_lora . A^T while the other CTAs run the GEMV.  Every warp of those
+// CTAs takes 16-column k-steps round robin (mma.sync m16n8k16: tokens x k
+// times k x adapter rows, fp32 accumulators; the loads of two k-steps are in
+// flight before their MMAs), and each CTA sums its warps in warp order into
+// its fp32 partial [M][r] in the workspace, then adds 1 to counters[0] with
+// release semantics.  Every GEMV CTA waits (acquire, bounded) until all
+// kNfDownCtas partials are in, sums them in CTA order and rounds once to
+// the activation dtype (the reference's lora_A(x) output) -- the same value
+// in every CTA.  The last GEMV CTA to finish zeroes counters[0] and [2]
+// again, so the counter area is zero at rest.  No CTA of this grid waits on
+// a later grid, and this grid's dependent launches only once every CTA of
+// it is resident, so the down CTAs always run.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits (at most kWaitLimit polls) until *p >= v; false if it gave up
+// (counted in g_kernel_timeouts).
+__device__ __forceinline__ bool count_wait(const unsigned* p, uint32_t v) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (ld_acquire_gpu(p) >= v) return true;
+    __nanosleep(32);
+  }
+  atomicAdd(&g_kernel_timeouts, 1u);
+  return false;
+}
+
+// shared memory of the down role: [warps][16 tokens][8 * ceil(r / 8)] fp32
+__host__ __device__ constexpr size_t down_smem(int r) {
+  return (size_t)(kNfBlockThreads / 32) * 16 * (size_t)(8 * ((r + 7) / 8)) * sizeof(float);
+}
+
+template <int DT, int NJ>
+__device__ __forceinline__ void down_kstep(const typename DType<DT>::T* x0, const typename DType<DT>::T* x1,
+                                           const typename DType<DT>::T* A, int K, int r, int nj, bool r0, bool r1,
+                                           int k0, int g, int t, uint32_t (&a)[4], uint32_t (&b)[NJ][2]) {
+  // x through L2 (the grid before may have written it), A through the
+  // read-only path (a weight)
+  a[0] = r0 ? __ldcg(reinterpret_cast<const unsigned*>(x0 + k0)) : 0u;
+  a[1] = r1 ? __ldcg(reinterpret_cast<const unsigned*>(x1 + k0)) : 0u;
+  a[2] = r0 ? __ldcg(reinterpret_cast<const unsigned*>(x0 + k0 + 8)) : 0u;
+  a[3] = r1 ? __ldcg(reinterpret_cast<const unsigned*>(x1 + k0 + 8)) : 0u;
+#pragma unroll
+  for (int jt = 0; jt < NJ; ++jt) {
+    const int j = jt * 8 + g;
+    const bool ok = jt < nj && j < r;
+    const unsigned* ar = reinterpret_cast<const unsigned*>(A + (size_t)(ok ? j : 0) * K + k0 + 2 * t);
+    b[jt][0] = ok ? __ldg(ar) : 0u;
+    b[jt][1] = ok ? __ldg(ar + 4) : 0u;
+  }
+}
+
+// NJ: 8-row tiles of A held (nj <= NJ); with NJ <= 4 the loads of two
+// k-steps are in flight before their MMAs
+template <int DT, int NJ>
+__device__ __noinline__ void down_role(const GemvArgs& p, unsigned char* smem) {
+  using T = typename DType<DT>::T;
+  constexpr int KB = NJ <= 4 ? 2 : 1;
+  constexpr int kW = kNfBlockThreads / 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int M = (int)p.M, K = (int)p.w.K, r = p.r, nj = (r + 7) >> 3, RP = 8 * nj;
+  const T* X = static_cast<const T*>(p.lora_x);
+  const T* A = static_cast<const T*>(p.lora_a);
+  const int d = blockIdx.x, W = kNfDownCtas * kW, nks = K >> 4;
+  // A is a weight: start this CTA's lines of it towards L2 before the wait
+  for (int e = tid; e < r * kW; e += kNfBlockThreads) {
+    const int j = e / kW, w = e - j * kW;
+    for (int ks = d * kW + w; ks < nks; ks += W)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(A + (size_t)j * K + ks * 16));
+  }
+  // x_lora may be the output of the grid before this one
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  float acc[NJ][4];
+#pragma unroll
+  for (int jt = 0; jt < NJ; ++jt) acc[jt][0] = acc[jt][1] = acc[jt][2] = acc[jt][3] = 0.0f;
+  const bool r0 = g < M, r1 = g + 8 < M;
+  const T* x0 = X + (size_t)(r0 ? g : 0) * K + 2 * t;
+  const T* x1 = X + (size_t)(r1 ? g + 8 : 0) * K + 2 * t;
+  for (int ks = d * kW + warp; ks < nks; ks += KB * W) {
+    uint32_t a[KB][4], b[KB][NJ][2];
+#pragma unroll
+    for (int i = 0; i < KB; ++i)
+      if (i == 0 || ks + i * W < nks) down_kstep<DT, NJ>(x0, x1, A, K, r, nj, r0, r1, (ks + i * W) * 16, g, t, a[i], b[i]);
+#pragma unroll
+    for (int i = 0; i < KB; ++i) {
+      if (i > 0 && ks + i * W >= nks) break;
+#pragma unroll
+      for (int jt = 0; jt < NJ; ++jt)
+        if (jt < nj) Mma16816<DT>::run(acc[jt], a[i][0], a[i][1], a[i][2], a[i][3], b[i][jt][0], b[i][jt][1]);
+    }
+  }
+  float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+  for (int jt = 0; jt < NJ; ++jt) {
+    if (jt < nj) {
+      float* r_lo = red + (warp * 16 + g) * RP + jt * 8 + 2 * t;
+      float* r_hi = red + (warp * 16 + g + 8) * RP + jt * 8 + 2 * t;
+      r_lo[0] = acc[jt][0], r_lo[1] = acc[jt][1], r_hi[0] = acc[jt][2], r_hi[1] = acc[jt][3];
+    }
+  }
+  __syncthreads();
+  float* part = p.partial + (size_t)d * M * r;
+  for (int e = tid; e < M * r; e += kNfBlockThreads) {
+    const int m = e / r, j = e - m * r;
+    float s = 0.0f;
+    for (int w = 0; w < kW; ++w) s += red[(w * 16 + m) * RP + j];
+    part[e] = s;
+  }
+  __syncthreads();  // every partial store of the CTA precedes the release below
+  if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.counters) : "memory");
+}
+
 // 2-D tiled TMA load of box (x, y) of `map` into shared memory, completing on `bar`
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -395,8 +520,19 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   // The next layer's down-product kernel (a programmatic dependent) may be
   // scheduled beside this grid now: it waits for this grid to finish before
-  // it reads anything or lets its own dependent start.
+  // it reads anything but weights.
   asm volatile("griddepcontrol.launch_dependents;");
+  // The gather's flags and counters are written by the calls before this
+  // one: a gather kernel waits for the grids before it at once.
+  if (q.a.gather) asm volatile("griddepcontrol.wait;" ::: "memory");
+  // fused LoRA down product: the grid's first kNfDownCtas CTAs
+  if (p.fuse_down && blockIdx.x < (unsigned)kNfDownCtas) {
+    if (p.r <= 16) down_role<DT, 2>(p, smem);
+    else if (p.r <= 32) down_role<DT, 4>(p, smem);
+    else down_role<DT, 8>(p, smem);
+    return;
+  }
+  const int cta = (int)blockIdx.x - (p.fuse_down ? kNfDownCtas : 0);  // GEMV CTA index
   const int N = (int)p.w.N, K = (int)p.w.K, M = (int)p.M;
   const int nbk = K >> 6;
   const int nst = (nbk + kStageBlocks - 1) / kStageBlocks;
@@ -417,7 +553,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   volatile int* raw_issuedp = &raw_issued;
   volatile int* donep = &producer_done;
 
-  const int tb = blockIdx.x * q.tpc;
+  const int tb = cta * q.tpc;
   const int te = tb + q.tpc < q.tiles ? tb + q.tpc : q.tiles;
   auto pass_tiles = [&](int ch, int& t0, int& t1) {
     t0 = tb + ch * NT;
@@ -449,10 +585,22 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     }
     __syncwarp();
     start_arrive();
-    // ---- stage u (over all passes) into slot u % S
+    // ---- stage u (over all passes) into slot u % S.  X may be the output
+    // of the grid this one overlaps: the first ring fill streams the codes
+    // only, and X of those stages follows once the grids before this one
+    // have finished (griddepcontrol.wait; gather kernels waited at start).
     if (lane == 0) {
       const uint32_t bytes = 2 * kBox + (uint32_t)M * 1024;
-      uint32_t u = 0;
+      uint32_t u = 0, xpend = 0;  // stages 0 .. xpend-1 of pass 0 still wait for X
+      bool xopen = p.gather != 0 || q.xsafe != 0;
+      const uint32_t fill = (uint32_t)(nst < S ? nst : S);
+      auto open_x = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (uint32_t v = 0; v < xpend; ++v)
+          tma_load_2d(ring + v * slot_bytes + 2 * kBox, &q.xmap, (int)v * 256, 0, full0 + 8 * v);
+        xpend = 0;
+        xopen = true;
+      };
       for (int ch = 0; ch < q.chunks && !*abortp; ++ch) {
         int t0, t1;
         pass_tiles(ch, t0, t1);
@@ -483,10 +631,16 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
             tma_load_2d(dst, &q.wmap, s * 256, t0 * 16, bar);
             tma_load_2d(dst + kBox, &q.wmap, s * 256 + 128, t0 * 16, bar);
           }
-          tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
+          if (xopen) {
+            tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
+          } else {
+            ++xpend;  // pass 0, stage s == u in slot u
+            if (xpend == fill) open_x();
+          }
           *issuedp = (int)(u + 1);
         }
       }
+      if (xpend) open_x();  // the loop ended early: every issued stage still completes
       __threadfence_block();
       *donep = 1;
     }
@@ -716,7 +870,16 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     }
     if (ch == 0) {
       asm volatile("griddepcontrol.wait;" ::: "memory");  // x.A^T of the kernel before
-      if (p.r > 0) {
+      if (p.fuse_down) {  // x.A^T from the partials of this grid's down CTAs
+        if (tid == 0 && !count_wait(p.counters, kNfDownCtas)) *abortp = 1;
+        consumer_sync();
+        for (int e = tid; e < M * p.r; e += kNfThreads) {
+          float sum = 0.0f;
+#pragma unroll
+          for (int c = 0; c < kNfDownCtas; ++c) sum += __ldcg(p.partial + (size_t)c * M * p.r + e);
+          tl[e] = DType<DT>::from_f32(sum);
+        }
+      } else if (p.r > 0) {
         const T* td = static_cast<const T*>(p.tdown);
         for (int e = tid; e < M * p.r; e += kNfThreads) tl[e] = td[e];
       }
@@ -804,6 +967,17 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     for (uint32_t v = passes; v < nr; ++v)
       for (uint32_t i = 0; i < kWaitLimit && !mbar_test(scfull, v & 1); ++i) {
       }
+  }
+  if (p.fuse_down && tid == 0) {
+    // the last GEMV CTA zeroes the counters once every GEMV CTA has read the
+    // partials (each arrives after its epilogue; an aborted CTA arrives too)
+    // and every down CTA has added its arrival
+    __threadfence();
+    if (atomicAdd(p.counters + 2, 1u) == gridDim.x - kNfDownCtas - 1u) {
+      count_wait(p.counters, kNfDownCtas);
+      p.counters[2] = 0u;
+      p.counters[0] = 0u;
+    }
   }
   if (p.gather) {
     // every consumer's stores of the call are ordered before the arrival by
@@ -935,12 +1109,12 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r, bool exact)
   return pl->smem;
 }
 
-static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool pdl, bool exact, Nf4Plan* pl) {
+static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool beside, bool exact, Nf4Plan* pl) {
   pl->mg = M > 8 ? 2 : 1;
   pl->esz = esz;
   const int64_t tiles = (N + 15) / 16;
   // with the down product running beside it, leave the SMs its cluster uses
-  int64_t G = num_sms() - (pdl ? kLoraDownCtas : 0);
+  int64_t G = num_sms() - (beside ? kLoraDownCtas : 0);
   if (G > tiles) G = tiles;
   if (G < 1) G = 1;
   const int64_t per = (tiles + G - 1) / G;
@@ -998,7 +1172,7 @@ bool gemv_nf4_fits(const QWeight& w, int64_t M, int r) {
 }
 
 template <int DT, int MG, int NT, bool EXACT>
-static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) {
+static int nf4_launch(const Nf4Args& q, size_t smem, cudaStream_t st) {
   auto kern = gemv_nf4_k<DT, MG, NT, EXACT>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
@@ -1011,7 +1185,7 @@ static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) 
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = 1;  // X and x.A^T are read only after griddepcontrol.wait
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q);
   if (e != cudaSuccess) {
     set_cuda_error(e);
@@ -1021,29 +1195,29 @@ static int nf4_launch(const Nf4Args& q, size_t smem, bool pdl, cudaStream_t st) 
 }
 
 template <int DT, int MG, bool EXACT>
-static int nf4_nt(const Nf4Args& q, int nt, size_t smem, bool pdl, cudaStream_t st) {
+static int nf4_nt(const Nf4Args& q, int nt, size_t smem, cudaStream_t st) {
   switch (nt) {
-    case 1: return nf4_launch<DT, MG, 1, EXACT>(q, smem, pdl, st);
-    case 2: return nf4_launch<DT, MG, 2, EXACT>(q, smem, pdl, st);
-    case 3: return nf4_launch<DT, MG, 3, EXACT>(q, smem, pdl, st);
-    case 4: return nf4_launch<DT, MG, 4, EXACT>(q, smem, pdl, st);
-    case 5: return nf4_launch<DT, MG, 5, EXACT>(q, smem, pdl, st);
+    case 1: return nf4_launch<DT, MG, 1, EXACT>(q, smem, st);
+    case 2: return nf4_launch<DT, MG, 2, EXACT>(q, smem, st);
+    case 3: return nf4_launch<DT, MG, 3, EXACT>(q, smem, st);
+    case 4: return nf4_launch<DT, MG, 4, EXACT>(q, smem, st);
+    case 5: return nf4_launch<DT, MG, 5, EXACT>(q, smem, st);
   }
   if constexpr (MG == 1)
-    if (nt == 6) return nf4_launch<DT, MG, 6, EXACT>(q, smem, pdl, st);
+    if (nt == 6) return nf4_launch<DT, MG, 6, EXACT>(q, smem, st);
   return RQ_ERR_INVALID;
 }
 
 template <int DT, bool EXACT>
-static int nf4_dispatch(const Nf4Args& q, const Nf4Plan& pl, bool pdl, cudaStream_t st) {
-  return pl.mg == 2 ? nf4_nt<DT, 2, EXACT>(q, pl.nt, pl.smem, pdl, st) : nf4_nt<DT, 1, EXACT>(q, pl.nt, pl.smem, pdl, st);
+static int nf4_dispatch(const Nf4Args& q, const Nf4Plan& pl, cudaStream_t st) {
+  return pl.mg == 2 ? nf4_nt<DT, 2, EXACT>(q, pl.nt, pl.smem, st) : nf4_nt<DT, 1, EXACT>(q, pl.nt, pl.smem, st);
 }
 
-int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
+int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st) {
   if (g.w.K % 64 || ((uintptr_t)g.w.q % 16) || ((uintptr_t)g.x % 16)) return RQ_ERR_ALIGN;
   Nf4Plan pl;
   const bool exact = decode_exact();
-  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), pdl, exact, &pl)) return RQ_ERR_INVALID;
+  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), beside, exact, &pl)) return RQ_ERR_INVALID;
   Nf4Args q;
   // codes with 128-byte swizzle: 3-D [N][K/256][128] bytes, box 128 x 2 x NT*16
   // when K % 256 == 0, else 2-D [N][K/2] bytes, box 128 x NT*16;
@@ -1062,7 +1236,7 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
                     &q.xmap);
   if (rc != RQ_OK) return rc;
   q.a = g;
-  q.a.grid = pl.grid;
+  q.a.grid = pl.grid + (g.fuse_down ? kNfDownCtas : 0);
   q.tiles = pl.tiles;
   q.tpc = pl.tpc;
   q.chunks = pl.chunks;
@@ -1079,9 +1253,13 @@ int gemv_nf4_forward(const GemvArgs& g, bool pdl, cudaStream_t st) {
   q.stg_off = pl.stg_off;
   q.bsm_off = pl.bsm_off;
   q.bsm = pl.chunks == 1 && g.r > 0 && g.r % 8 == 0 && ((uintptr_t)g.lora_b % 16) == 0;
+  // behind a separate down-product kernel X is complete at launch; with the
+  // down product fused, the grid before may still be writing X
+  q.xsafe = g.r > 0 && !g.fuse_down;
+  if (g.fuse_down && down_smem(g.r) > pl.smem) pl.smem = down_smem(g.r);
   if (g.xdt == RQ_BF16)
-    return exact ? nf4_dispatch<RQ_BF16, true>(q, pl, pdl, st) : nf4_dispatch<RQ_BF16, false>(q, pl, pdl, st);
-  return exact ? nf4_dispatch<RQ_F16, true>(q, pl, pdl, st) : nf4_dispatch<RQ_F16, false>(q, pl, pdl, st);
+    return exact ? nf4_dispatch<RQ_BF16, true>(q, pl, st) : nf4_dispatch<RQ_BF16, false>(q, pl, st);
+  return exact ? nf4_dispatch<RQ_F16, true>(q, pl, st) : nf4_dispatch<RQ_F16, false>(q, pl, st);
 }
 
 }  // namespace rq

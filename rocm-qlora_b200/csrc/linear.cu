@@ -107,13 +107,19 @@ int linear_forward(const LinearArgs& a, cudaStream_t st) {
   int rc = carve(a, &v);
   if (rc != RQ_OK) return rc;
   if (a.M == 0 || a.w.N == 0) return RQ_OK;
+  LinearArgs g = a;
+  g.M = a.M < 16 ? a.M : 16;
+  const bool gemv = gemv_supported(g);
+  if (gemv && a.M <= 16 && gemv_fuse_down(a)) {
+    // one launch: the NF4 GEMV's grid computes x.A^T beside the main loop
+    t_last_path = RQ_PATH_GEMV;
+    return gemv_forward(a, v.t, st, v.partial, v.counters);
+  }
   if (a.r > 0) {
     rc = lora_down_any(a, false, a.lora_x, a.w.K, a.lora_a, 1.0f, false, v, st);
     if (rc != RQ_OK) return rc;
   }
-  LinearArgs g = a;
-  g.M = a.M < 16 ? a.M : 16;
-  if (gemv_supported(g)) {
+  if (gemv) {
     if (a.M <= 16) {
       t_last_path = RQ_PATH_GEMV;
       return gemv_forward(a, v.t, st);

@@ -137,29 +137,48 @@ static int launch_nf4_quantize(const void* x, int64_t n, int bs, uint8_t* packed
 
 // -------------------------------------------------------------- NF4 dequant
 // Each thread expands 8 packed bytes (16 values).  Blocks of >= 16 elements
-// that are multiples of 16 keep one scale per thread chunk.
-template <int SDT, int ODT>
-__global__ void __launch_bounds__(256) nf4_dequantize_k(const uint8_t* __restrict__ packed, int64_t nbytes,
-                                                        const typename DType<SDT>::T* __restrict__ scales,
-                                                        int bs, typename DType<ODT>::T* __restrict__ out) {
+// that are multiples of 16 keep one scale per thread chunk.  The block scale
+// comes from a scale source: the plain per-block scales, or (double quant)
+// the second-level code times its group's c2_scales entry.
+template <int SDT>
+struct PlainScales {
+  const typename DType<SDT>::T* s;
+  __device__ __forceinline__ float operator()(int64_t b) const { return DType<SDT>::to_f32(s[b]); }
+};
+// double_dequantize (double_quant.py:99-122): c1 = decode(c2) * c2_scales
+struct DqScales {
+  const uint8_t* c2;
+  const float* c2s;
+  int fp8, bs2;
+  __device__ __forceinline__ float operator()(int64_t b) const {
+    const float q = fp8 ? e4m3fnuz_to_f32(c2[b]) : ieee_div((float)(int8_t)c2[b], 127.0f);
+    return q * c2s[b / bs2];
+  }
+};
+
+template <class SF, int ODT>
+__global__ void __launch_bounds__(256) nf4_dequantize_k(const uint8_t* __restrict__ packed, int64_t nv,
+                                                        const SF sf, int bs,
+                                                        typename DType<ODT>::T* __restrict__ out) {
+  // nv values (packed holds ceil(nv / 2) bytes)
   __shared__ float lut[16];
   if (threadIdx.x < 16) lut[threadIdx.x] = kNF4[threadIdx.x];
   __syncthreads();
-  const int64_t nchunks = (nbytes + 7) / 8;
+  const int64_t nchunks = (nv + 15) / 16;
   const bool fast_scale = (bs % 16) == 0;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
        c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b0 = c * 8;
     const int64_t e0 = b0 * 2;
-    if (b0 + 8 <= nbytes && ((uintptr_t)(packed + b0) % 8 == 0)) {
+    if (e0 + 16 <= nv && ((uintptr_t)(packed + b0) % 8 == 0)) {
       const uint2 raw = *reinterpret_cast<const uint2*>(packed + b0);
       const uint32_t w[2] = {raw.x, raw.y};
-      float s = fast_scale ? DType<SDT>::to_f32(scales[e0 / bs]) : 0.0f;
+      const float s = fast_scale ? sf(e0 / bs) : 0.0f;
       float v[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int code = (w[i / 8] >> (4 * (i % 8))) & 0xF;
-        const float si = fast_scale ? s : DType<SDT>::to_f32(scales[(e0 + i) / bs]);
+        const float si = fast_scale ? s : sf((e0 + i) / bs);
         v[i] = lut[code] * si;
       }
       if constexpr (ODT == RQ_F32) {
@@ -185,32 +204,12 @@ __global__ void __launch_bounds__(256) nf4_dequantize_k(const uint8_t* __restric
         }
       }
     } else {
-      for (int64_t i = e0; i < 2 * nbytes && i < e0 + 16; ++i) {
+      for (int64_t i = e0; i < nv && i < e0 + 16; ++i) {
         const uint8_t byte = packed[i >> 1];
         const int code = (i & 1) ? (byte >> 4) : (byte & 0xF);
-        out[i] = DType<ODT>::from_f32(lut[code] * DType<SDT>::to_f32(scales[i / bs]));
+        out[i] = DType<ODT>::from_f32(lut[code] * sf(i / bs));
       }
     }
-  }
-}
-
-// --------------------------------------------------- double-quant dequant
-template <int ODT>
-__global__ void __launch_bounds__(256) dq_dequantize_k(const uint8_t* __restrict__ packed, int64_t numel,
-                                                       const uint8_t* __restrict__ c2,
-                                                       const float* __restrict__ c2s, int fp8, int bs,
-                                                       int bs2, typename DType<ODT>::T* __restrict__ out) {
-  __shared__ float lut[16];
-  if (threadIdx.x < 16) lut[threadIdx.x] = kNF4[threadIdx.x];
-  __syncthreads();
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = i / bs;
-    const float q = fp8 ? e4m3fnuz_to_f32(c2[b]) : ieee_div((float)(int8_t)c2[b], 127.0f);
-    const float s = q * c2s[b / bs2];
-    const uint8_t byte = packed[i >> 1];
-    const int code = (i & 1) ? (byte >> 4) : (byte & 0xF);
-    out[i] = DType<ODT>::from_f32(lut[code] * s);
   }
 }
 
@@ -319,9 +318,37 @@ __global__ void __launch_bounds__(256) int8_dequantize_k(const int8_t* __restric
                                                          const typename DType<SDT>::T* __restrict__ scales,
                                                          int bs, int64_t cols,
                                                          typename DType<ODT>::T* __restrict__ out) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t si = cols > 0 ? i / cols : i / bs;
-    out[i] = DType<ODT>::from_f32((float)q[i] * DType<SDT>::to_f32(scales[si]));
+  // 16 values a thread: one 16-byte load, one scale when the scale
+  // period (cols, or bs) is a multiple of 16
+  const int64_t per = cols > 0 ? cols : (int64_t)bs;
+  const bool one_scale = per % 16 == 0;
+  const int64_t nchunks = (n + 15) / 16;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = c * 16;
+    if (one_scale && e0 + 16 <= n && ((uintptr_t)(q + e0) % 16) == 0 && ((uintptr_t)(out + e0) % 16) == 0) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(q + e0);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      const float s = DType<SDT>::to_f32(scales[e0 / per]);
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = (float)(int8_t)(w[i / 4] >> (8 * (i % 4))) * s;
+      if constexpr (ODT == RQ_F32) {
+        float4* o = reinterpret_cast<float4*>(out + e0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      } else {
+        uint32_t h[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = pack2<ODT>(v[2 * i], v[2 * i + 1]);
+        uint4* o = reinterpret_cast<uint4*>(out + e0);
+        o[0] = make_uint4(h[0], h[1], h[2], h[3]);
+        o[1] = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+    } else {
+      for (int64_t i = e0; i < n && i < e0 + 16; ++i)
+        out[i] = DType<ODT>::from_f32((float)q[i] * DType<SDT>::to_f32(scales[i / per]));
+    }
   }
 }
 
@@ -347,13 +374,14 @@ template <int SDT>
 static int nf4_deq_s(const uint8_t* p, int64_t nbytes, const void* s, int bs, void* out, int odt,
                      cudaStream_t st) {
   const int g = grid_1d((nbytes + 7) / 8);
-  const auto* sp = static_cast<const typename DType<SDT>::T*>(s);
+  const PlainScales<SDT> sp{static_cast<const typename DType<SDT>::T*>(s)};
+  const int64_t nv = 2 * nbytes;
   switch (odt) {
-    case RQ_F32: nf4_dequantize_k<SDT, RQ_F32><<<g, 256, 0, st>>>(p, nbytes, sp, bs, (float*)out); break;
+    case RQ_F32: nf4_dequantize_k<PlainScales<SDT>, RQ_F32><<<g, 256, 0, st>>>(p, nv, sp, bs, (float*)out); break;
     case RQ_BF16:
-      nf4_dequantize_k<SDT, RQ_BF16><<<g, 256, 0, st>>>(p, nbytes, sp, bs, (__nv_bfloat16*)out);
+      nf4_dequantize_k<PlainScales<SDT>, RQ_BF16><<<g, 256, 0, st>>>(p, nv, sp, bs, (__nv_bfloat16*)out);
       break;
-    case RQ_F16: nf4_dequantize_k<SDT, RQ_F16><<<g, 256, 0, st>>>(p, nbytes, sp, bs, (__half*)out); break;
+    case RQ_F16: nf4_dequantize_k<PlainScales<SDT>, RQ_F16><<<g, 256, 0, st>>>(p, nv, sp, bs, (__half*)out); break;
     default: return RQ_ERR_DTYPE;
   }
   return check_launch();
@@ -371,13 +399,14 @@ int nf4_dequantize(const uint8_t* p, int64_t nbytes, const void* s, int sdt, int
 
 int dq_dequantize(const uint8_t* p, int64_t numel, const uint8_t* c2, const float* c2s, int fp8, int bs,
                   int bs2, void* out, int odt, cudaStream_t st) {
-  const int g = grid_1d(numel);
+  const int g = grid_1d((numel + 15) / 16);
+  const DqScales sf{c2, c2s, fp8, bs2};
   switch (odt) {
-    case RQ_F32: dq_dequantize_k<RQ_F32><<<g, 256, 0, st>>>(p, numel, c2, c2s, fp8, bs, bs2, (float*)out); break;
+    case RQ_F32: nf4_dequantize_k<DqScales, RQ_F32><<<g, 256, 0, st>>>(p, numel, sf, bs, (float*)out); break;
     case RQ_BF16:
-      dq_dequantize_k<RQ_BF16><<<g, 256, 0, st>>>(p, numel, c2, c2s, fp8, bs, bs2, (__nv_bfloat16*)out);
+      nf4_dequantize_k<DqScales, RQ_BF16><<<g, 256, 0, st>>>(p, numel, sf, bs, (__nv_bfloat16*)out);
       break;
-    case RQ_F16: dq_dequantize_k<RQ_F16><<<g, 256, 0, st>>>(p, numel, c2, c2s, fp8, bs, bs2, (__half*)out); break;
+    case RQ_F16: nf4_dequantize_k<DqScales, RQ_F16><<<g, 256, 0, st>>>(p, numel, sf, bs, (__half*)out); break;
     default: return RQ_ERR_DTYPE;
   }
   return check_launch();
@@ -425,7 +454,7 @@ int int8_quantize_rows(const void* x, int dtype, int64_t rows, int64_t cols, int
 template <int SDT>
 static int int8_deq_s(const int8_t* q, int64_t n, const void* s, int bs, int64_t cols, void* out, int odt,
                       cudaStream_t st) {
-  const int g = grid_1d(n);
+  const int g = grid_1d((n + 15) / 16);
   const auto* sp = static_cast<const typename DType<SDT>::T*>(s);
   switch (odt) {
     case RQ_F32: int8_dequantize_k<SDT, RQ_F32><<<g, 256, 0, st>>>(q, n, sp, bs, cols, (float*)out); break;

@@ -89,7 +89,10 @@ int lora_down(int dt, bool w_transposed, const void* X, int64_t M, int64_t Kr, c
 int simt_forward(const LinearArgs& a, const void* tdown, cudaStream_t st);
 int simt_dx(const LinearArgs& a, const void* gt, cudaStream_t st);
 bool gemv_supported(const LinearArgs& a);
-int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st);
+bool gemv_fuse_down(const LinearArgs& a);
+// `partial` / `counters` (workspace): the NF4 GEMV computes tdown itself
+int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st, float* partial = nullptr,
+                 unsigned* counters = nullptr);
 
 int linear_forward(const LinearArgs& a, cudaStream_t st);
 int merge_weight(const QWeight& w, const float* A, const float* B, int r, float s, int mode, void* out, int odt,
