@@ -176,6 +176,25 @@ RQ_API int rq_merge_lora(int wfmt, const void* qweight, const void* scales, int 
                   const float* lora_a, const float* lora_b, int r, float scaling, int mode,
                   void* out, int out_dtype, void* stream);
 
+/* The quantized weight as a per-tensor scaled float8_e4m3fn GEMM operand
+ * (FP8LinearWrapper's native path, rocm_qlora/fp8/fp8_linear.py:27-39):
+ *   rq_weight_absmax: *absmax (device fp32) = max |rnd(deq(W))|, the weight
+ *     rounded to `dtype` (the activation dtype, RQ_BF16 / RQ_F16 / RQ_F32);
+ *   rq_weight_to_fp8: fp8_out[n*K + k] = e4m3fn(rnd(rnd(deq(W)[n, k]) / rnd(w_scale)))
+ *     (as torch divides a `dtype` tensor by a 0-dim fp32 GPU tensor: the
+ *     divisor rounded to `dtype`, the division in fp32 rounded to `dtype`;
+ *     then round-to-nearest-even to e4m3fn without saturation), N*K bytes
+ *     row-major.
+ * The reference computes w_scale = absmax / 448 (e4m3fn's largest value). */
+RQ_API int rq_weight_absmax(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                     const uint8_t* c2, const float* c2_scales,
+                     int64_t N, int64_t K, int block_size, int dtype,
+                     float* absmax, void* stream);
+RQ_API int rq_weight_to_fp8(int wfmt, const void* qweight, const void* scales, int scale_dtype,
+                     const uint8_t* c2, const float* c2_scales,
+                     int64_t N, int64_t K, int block_size, int dtype, float w_scale,
+                     uint8_t* fp8_out, void* stream);
+
 /* Bytes of device scratch compiled into the library for
  * rq_linear_forward_noalloc (held on every GPU that loads the library). */
 #define RQ_NOALLOC_SCRATCH_BYTES (2u << 20)

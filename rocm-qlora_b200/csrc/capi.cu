@@ -116,7 +116,7 @@ using namespace rq;
 
 extern "C" {
 
-int rq_abi_version(void) { return 2; }
+int rq_abi_version(void) { return 3; }
 
 const char* rq_status_string(int s) {
   switch (s) {
@@ -276,6 +276,31 @@ int rq_merge_lora(int wfmt, const void* qweight, const void* scales, int scale_d
   if ((uintptr_t)out % dtype_size(out_dtype)) return RQ_ERR_ALIGN;
   const QWeight w{wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size};
   return merge_weight(w, lora_a, lora_b, r, scaling, mode, out, out_dtype, (cudaStream_t)stream);
+}
+
+int rq_weight_absmax(int wfmt, const void* qweight, const void* scales, int scale_dtype, const uint8_t* c2,
+                     const float* c2_scales, int64_t N, int64_t K, int block_size, int dtype, float* absmax,
+                     void* stream) {
+  RQ_PROLOGUE();
+  const int rc = check_weight(wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size);
+  if (rc != RQ_OK) return rc;
+  if (!dtype_ok(dtype)) return RQ_ERR_DTYPE;
+  if (!absmax) return RQ_ERR_INVALID;
+  if ((uintptr_t)absmax % 4) return RQ_ERR_ALIGN;
+  const QWeight w{wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size};
+  return weight_absmax(w, dtype, absmax, (cudaStream_t)stream);
+}
+
+int rq_weight_to_fp8(int wfmt, const void* qweight, const void* scales, int scale_dtype, const uint8_t* c2,
+                     const float* c2_scales, int64_t N, int64_t K, int block_size, int dtype, float w_scale,
+                     uint8_t* fp8_out, void* stream) {
+  RQ_PROLOGUE();
+  const int rc = check_weight(wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size);
+  if (rc != RQ_OK) return rc;
+  if (!dtype_ok(dtype)) return RQ_ERR_DTYPE;
+  if (N * K > 0 && !fp8_out) return RQ_ERR_INVALID;
+  const QWeight w{wfmt, qweight, scales, scale_dtype, c2, c2_scales, N, K, block_size};
+  return weight_to_fp8(w, dtype, w_scale, fp8_out, (cudaStream_t)stream);
 }
 
 void launch_int4_dequant_matmul(void* stream, void* x, void* w_packed, void* scales, void* c, int M, int N, int K,

@@ -15,6 +15,62 @@ namespace rq {
 
 // ---------------------------------------------------------------- NF4 quant
 //
+// For bf16 / f16 inputs the normalized value x / absmax is a 16-bit value in
+// [-1, 1] (|x| <= absmax, absmax >= 1e-12 after the clamp), or NaN.  Its code
+// nf4_code(value) then depends only on the 16-bit pattern: every |value| <
+// 2^-5 lies between the thresholds of code 7, and the patterns from 2^-5 to
+// 1 are few (641 bf16, 5121 f16 a sign).  A per-CTA table holds
+//   entry 0                 code 7 (|value| < 2^-5)
+//   entry 1 + (a - lo)      nf4_code of pattern a, lo <= a <= 1.0
+//   entry 2 + (1.0 - lo)    code 0 (NaN; +inf cannot occur)
+// for each sign, built with nf4_code itself, so a lookup equals nf4_code
+// for every value the kernel can meet.
+template <int DT> struct QTab;
+template <> struct QTab<RQ_BF16> {
+  static constexpr uint32_t kLo = 0x3D00u, kOne = 0x3F80u, kSign = 0x400u, kSize = 2 * kSign;
+  static __device__ __forceinline__ uint32_t bits(float q) { return __bfloat16_as_ushort(__float2bfloat16_rn(q)); }
+  static __device__ __forceinline__ float value(uint32_t b) { return __uint_as_float(b << 16); }
+  static __device__ __forceinline__ uint32_t sign(uint32_t b) { return (b >> 5) & kSign; }
+};
+template <> struct QTab<RQ_F16> {
+  static constexpr uint32_t kLo = 0x2800u, kOne = 0x3C00u, kSign = 0x2000u, kSize = 2 * kSign;
+  static __device__ __forceinline__ uint32_t bits(float q) { return __half_as_ushort(__float2half_rn(q)); }
+  static __device__ __forceinline__ float value(uint32_t b) {
+    return __half2float(__ushort_as_half((unsigned short)b));
+  }
+  static __device__ __forceinline__ uint32_t sign(uint32_t b) { return (b >> 2) & kSign; }
+};
+template <> struct QTab<RQ_F32> {  // fp32 inputs keep the threshold search
+  static constexpr uint32_t kSize = 4;
+};
+
+template <int DT>
+__device__ __forceinline__ void qtab_build(uint8_t* tab) {
+  using Q = QTab<DT>;
+  for (uint32_t e = threadIdx.x; e < Q::kSize; e += blockDim.x) {
+    const uint32_t j = e & (Q::kSign - 1), neg = e & Q::kSign;
+    int c = 0;
+    if (j == 0) {
+      c = 7;
+    } else if (j <= Q::kOne - Q::kLo + 1) {
+      const uint32_t a = Q::kLo + j - 1;
+      c = nf4_code(Q::value(neg ? (a | 0x8000u) : a));
+    }
+    tab[e] = (uint8_t)c;
+  }
+}
+
+// code of x / scale (the reference's x_norm, rounded to DT) from the table
+template <int DT>
+__device__ __forceinline__ int qtab_code(float q, const uint8_t* tab) {
+  using Q = QTab<DT>;
+  const uint32_t b = Q::bits(q), a = b & 0x7FFFu;
+  int j = (int)a - (int)(Q::kLo - 1);
+  j = j < 0 ? 0 : j;
+  j = j > (int)(Q::kOne - Q::kLo + 2) ? (int)(Q::kOne - Q::kLo + 2) : j;
+  return tab[(uint32_t)j | Q::sign(b)];
+}
+
 // Fast path: VEC = 16/sizeof(T) elements per lane, L = bs/VEC lanes per
 // block (L in {1,...,32}).  Each warp covers 32*VEC elements = 32/L blocks.
 template <int DT, int L>
@@ -24,6 +80,11 @@ __global__ void __launch_bounds__(256) nf4_quantize_vec(const typename DType<DT>
   using T = typename DType<DT>::T;
   constexpr int VEC = 16 / sizeof(T);
   constexpr int BS = VEC * L;
+  __shared__ uint8_t qtab[QTab<DT>::kSize];
+  if constexpr (DT != RQ_F32) {
+    qtab_build<DT>(qtab);
+    __syncthreads();
+  }
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -56,7 +117,9 @@ __global__ void __launch_bounds__(256) nf4_quantize_vec(const typename DType<DT>
       uint32_t bytes[VEC / 8 > 0 ? VEC / 8 : 1] = {0};
 #pragma unroll
       for (int i = 0; i < VEC; ++i) {
-        const int c = nf4_code(round_to<DT>(ieee_div(v[i], scale)));
+        int c;
+        if constexpr (DT == RQ_F32) c = nf4_code(ieee_div(v[i], scale));
+        else c = qtab_code<DT>(ieee_div(v[i], scale), qtab);
         bytes[i / 8] |= (uint32_t)c << (4 * (i % 8));
       }
       if constexpr (VEC == 4) {
@@ -114,7 +177,8 @@ static int launch_nf4_quantize(const void* x, int64_t n, int bs, uint8_t* packed
   const int threads = 256;
   auto grid_for = [&](int64_t warps_needed) {
     int64_t g = (warps_needed * 32 + threads - 1) / threads;
-    return (int)(g < 148 * 64 ? (g < 1 ? 1 : g) : 148 * 64);
+    // a persistent grid (8 CTAs an SM): each CTA builds its code table once
+    return (int)(g < 148 * 8 ? (g < 1 ? 1 : g) : 148 * 8);
   };
   const T* xp = static_cast<const T*>(x);
   T* sp = static_cast<T*>(scales);

@@ -95,6 +95,8 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st, float*
                  unsigned* counters = nullptr);
 
 int linear_forward(const LinearArgs& a, cudaStream_t st);
+int weight_absmax(const QWeight& w, int dt, float* out, cudaStream_t st);
+int weight_to_fp8(const QWeight& w, int dt, float s, uint8_t* out, cudaStream_t st);
 int merge_weight(const QWeight& w, const float* A, const float* B, int r, float s, int mode, void* out, int odt,
                  cudaStream_t st);
 int linear_dx(const LinearArgs& a, cudaStream_t st);

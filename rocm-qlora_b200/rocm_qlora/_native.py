@@ -59,6 +59,8 @@ def _bind(L: ctypes.CDLL) -> None:
         "rq_last_path": ([], I),
         "rq_set_decode_exact": ([I], None),
         "rq_merge_lora": ([I, P, P, I, P, P, I64, I64, I, P, P, I, F, I, P, I, P], I),
+        "rq_weight_absmax": ([I, P, P, I, P, P, I64, I64, I, I, P, P], I),
+        "rq_weight_to_fp8": ([I, P, P, I, P, P, I64, I64, I, I, F, P, P], I),
         "rq_take_kernel_timeouts": ([P], I),
         "rq_nf4_quantize": ([P, I, I64, I, P, P, P], I),
         "rq_nf4_dequantize": ([P, I64, P, I, I, P, I, P], I),
@@ -90,7 +92,7 @@ def _bind(L: ctypes.CDLL) -> None:
 def exported_symbols() -> Tuple[str, ...]:
     """Names of the C entry points this binding declares."""
     return ("rq_abi_version", "rq_status_string", "rq_last_cuda_error", "rq_last_status", "rq_last_path",
-            "rq_set_decode_exact", "rq_merge_lora",
+            "rq_set_decode_exact", "rq_merge_lora", "rq_weight_absmax", "rq_weight_to_fp8",
             "rq_take_kernel_timeouts",
             "rq_nf4_quantize", "rq_nf4_dequantize", "rq_int8_quantize", "rq_int8_quantize_rows",
             "rq_int8_dequantize", "rq_dq_quantize_scales", "rq_dq_dequantize",

@@ -37,7 +37,7 @@ def test_library_is_sm100a():
     build log's target list, not by decoding the binary)."""
     from rocm_qlora import _native as nat
     L = nat.load_library()
-    assert L.rq_abi_version() == 2
+    assert L.rq_abi_version() == 3
     mk = open(os.path.join(ROOT, "rocm-qlora_b200", "Makefile")).read()
     assert "arch=compute_100a,code=sm_100a" in mk
 
