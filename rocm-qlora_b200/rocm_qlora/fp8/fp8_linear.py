@@ -42,6 +42,17 @@ from rocm_qlora.quantization import layer_ops
 from rocm_qlora.quantization.quant_linear import QuantLinear
 
 _FP8_MAX = 448.0  # largest float8_e4m3fn value
+_fp8_max_t: Dict[torch.device, torch.Tensor] = {}
+
+
+def _fp8_max_on(dev: torch.device) -> torch.Tensor:
+    """448 as a 0-dim fp32 tensor on dev: dividing by it is an IEEE fp32
+    division (dividing by the Python number takes torch's scalar path, a
+    multiplication by the reciprocal, which can be one ulp off)."""
+    t = _fp8_max_t.get(dev)
+    if t is None:
+        t = _fp8_max_t[dev] = torch.full((), _FP8_MAX, dtype=torch.float32, device=dev)
+    return t
 
 
 def weight_fp8(w: layer_ops.WeightView, dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -75,7 +86,9 @@ class _FP8LinearFunc(torch.autograd.Function):
         ctx.x_shape = x.shape
         x2 = x.reshape(-1, x.shape[-1])
         f8 = get_fp8_dtype("e4m3")
-        x_scale = (x2.abs().amax().float() / _FP8_MAX).reshape(())
+        # max|x| / 448 correctly rounded to fp32, as the reference's
+        # double division of .item() stored as fp32 (no host sync here)
+        x_scale = (x2.abs().amax().float() / _fp8_max_on(x.device)).reshape(())
         x_f8 = (x2 / x_scale).to(f8)
         out = torch._scaled_mm(x_f8, w_f8.t(), scale_a=x_scale, scale_b=w_scale, out_dtype=x.dtype)
         out = out.reshape(*x.shape[:-1], -1)
