@@ -4,8 +4,10 @@
 //
 // Forward  Y[M, N]  = X[M, K] . deq(W[N, K])^T (+ bias, + LoRA), and the
 // transposed variant for backward  dX[M, K] = dY[M, N] . deq(W) (+ LoRA),
-// for M >= 64, bf16/f16 activations, NF4 weights (plain, fp8 or int8
-// double-quantized scales).
+// bf16/f16 activations, NF4 weights (plain, fp8 or int8 double-quantized
+// scales): the forward for M >= 64 (below that the decode GEMV in slabs of
+// 16 rows is faster), dX for every M (token rows past M arrive zero-filled
+// by the TMA bounds and are not written).
 //
 // A cluster of two CTAs (one per SM) computes a 256 (tokens) x BN (outputs)
 // tile, BN = 256 or 128, with tcgen05.mma.cta_group::2 (M = 256): each CTA
@@ -1005,7 +1007,7 @@ __global__ void __launch_bounds__(kLdThreads, 1) lora_down_tc_k(const __grid_con
 // ---------------------------------------------------------------- host side
 
 bool gemm_supported(const LinearArgs& a, bool dx) {
-  if (a.M < 64 || a.w.K % 64) return false;
+  if (a.M < (dx ? 1 : 64) || a.w.K % 64) return false;
   if (is_nf4_fmt(a.w.fmt) || a.w.fmt == RQ_W_INT8) {
     if (a.w.bs != 64) return false;  // one quant block a row and step
   } else if (a.w.fmt != RQ_W_INT8_ROW) {

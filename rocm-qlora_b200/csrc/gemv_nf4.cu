@@ -71,7 +71,7 @@
 namespace rq {
 
 constexpr int kStageBlocks = 8;                   // 64-blocks per stage (one per consumer warp pair)
-constexpr int kNfSplit = 2;                       // consumer warps per block column (they split the tiles)
+constexpr int kNfSplit = 2;                       // consumer warps per block column (they split the stages)
 constexpr int kNfWarps = kStageBlocks * kNfSplit;  // consumer warps
 constexpr int kNfThreads = kNfWarps * 32;
 constexpr int kNfBlockThreads = kNfThreads + 32;  // + the producer warp
@@ -84,6 +84,12 @@ constexpr size_t kNfSmemMax = 227 * 1024 - 256;   // dynamic shared memory (stat
 constexpr int kNfMaxNT1 = 6;                      // 16-row tiles per pass, M <= 8
 constexpr int kNfMaxNT2 = 5;                      // 16-row tiles per pass, M > 8
 constexpr int kNfMaxSlots = 8;                    // ring stages
+// The two consumer warps of a block column may split the stages (each holds
+// all the pass's tiles: half the per-stage waits and bookkeeping a tile)
+// unless a 16-token pass has 4 or more tiles, whose accumulators would not
+// fit in registers; they split the tiles then, and when the ring is shorter
+// than 4 stages (gemv_nf4_forward decides).
+__host__ __device__ constexpr bool nf4_stage_split(int mg, int nt) { return !(mg == 2 && nt >= 4); }
 
 // Bounded waits that ran out (a kernel that stopped early).
 __device__ unsigned int g_kernel_timeouts;
@@ -201,6 +207,7 @@ struct Nf4Args {
   int sp;            // floats per block row of the staged scales (NT * 16 + 2)
   int esz;           // bytes per raw scale (1: c2 codes; 2/4: plain scales)
   int wide;          // 1: 3-D code box (K % 256 == 0)
+  int stage_split;   // 1: the two warps of a block column split the stages (nf4_stage_split)
   int xsafe;         // 1: X is complete when this grid launches (it follows the
                      // down-product kernel, which lets it launch only after
                      // its own griddepcontrol.wait), so X is loaded at once
@@ -509,7 +516,7 @@ __host__ __device__ __forceinline__ int mma_row(int g, int wide) { return wide ?
 // MMA row of tile row rr (0..15) modulo 8
 __host__ __device__ __forceinline__ int mma_of_row(int rr, int wide) { return wide ? (rr & 7) : ((rr & 7) >> 1) + 4 * (rr & 1); }
 
-template <int DT, int MG, int NT, bool EXACT>
+template <int DT, int MG, int NT, bool EXACT, bool SS>
 __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_constant__ Nf4Args q) {
   using T = typename DType<DT>::T;
   const GemvArgs& p = q.a;
@@ -573,7 +580,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       asm volatile("prefetch.tensormap [%0];" ::"l"(&q.xmap) : "memory");
       for (int i = 0; i < S; ++i) {
         mbar_init(full0 + 8 * i, 1);
-        mbar_init(empty0 + 8 * i, kNfWarps);
+        mbar_init(empty0 + 8 * i, SS ? kStageBlocks : kNfWarps);  // the warps that take the stage
       }
       mbar_init(scfull, 1);
       mbar_init(scempty, 1);
@@ -672,7 +679,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   // (a tile is 16 or 32 shared rows: the swizzle phase repeats per tile)
   const uint32_t tstep = wide ? 4096u : 2048u, hstep = tstep / 2;
   const uint32_t cofs =
-      th * tstep + (wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
+      (wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
                          : (uint32_t)half * kBox + pg * 128 + (((lch ^ pg) << 4) | ((t & 1) << 3)));
   // lane's X in a slot: token gr*8 + g (tokens past M read token M-1, results
   // dropped), columns of block bw, 16 t .. 16 t + 15
@@ -777,18 +784,25 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     consumer_sync();
     if (tid == 0) mbar_arrive(scempty);
 
-    // this warp's tiles: nt = th + kNfSplit * i for i < NTW (nt < NT)
-    constexpr int NTW = (NT + kNfSplit - 1) / kNfSplit;
+    // stage split: this warp takes stages s = th, th + 2, ... and every tile
+    // of the pass; tile split (16-token passes of 4+ tiles, whose
+    // accumulators would not fit in registers): every stage, tiles
+    // nt = th + 2i
+    static_assert(!SS || nf4_stage_split(MG, NT), "stage split holds every tile's accumulators");
+    constexpr int NTW = SS ? NT : (NT + kNfSplit - 1) / kNfSplit;
     float acc[NTW][MG][4];
 #pragma unroll
     for (int i = 0; i < NTW; ++i)
 #pragma unroll
       for (int gr = 0; gr < MG; ++gr) acc[i][gr][0] = acc[i][gr][1] = acc[i][gr][2] = acc[i][gr][3] = 0.0f;
-    const float* scw = sc + bw * sp + th * 16 + g * 2;
+    const float* scw = sc + bw * sp + (SS ? 0 : th * 16) + g * 2;
+    const uint32_t cofs_w = cofs + (SS ? 0u : th * tstep);
 
     for (int s = 0; s < nst; ++s, ++u) {
-      const uint32_t slot = cslot;
-      const bool ok = mbar_wait(full0 + 8 * slot, cphase, abortp);
+      const uint32_t slot = cslot, par = cphase;
+      if (++cslot == (uint32_t)S) cslot = 0, cphase ^= 1u;
+      if (SS && (s & (kNfSplit - 1)) != th) continue;
+      const bool ok = mbar_wait(full0 + 8 * slot, par, abortp);
       const int b = s * kStageBlocks + bw;
       if (ok && b < nbk) {
         const uint32_t sl = ring + slot * slot_bytes;
@@ -804,12 +818,14 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         const float* sb = scw + (size_t)s * kStageBlocks * sp;
 #pragma unroll
         for (int i = 0; i < NTW; ++i) {
-          const int nt = th + kNfSplit * i;
-          if (NT % kNfSplit != 0 && nt >= NT) break;
+          constexpr int kStep = SS ? 1 : kNfSplit;  // tile stride of this warp's tiles
+          if (!SS && NT % kNfSplit != 0 && th + kNfSplit * i >= NT) break;
           uint2 lo, hi;
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs + i * kNfSplit * tstep));
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(hi.x), "=r"(hi.y) : "r"(sl + cofs + i * kNfSplit * tstep + hstep));
-          const float2 sv = *reinterpret_cast<const float2*>(sb + i * kNfSplit * 16);
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs_w + i * kStep * tstep));
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];"
+                       : "=r"(hi.x), "=r"(hi.y)
+                       : "r"(sl + cofs_w + i * kStep * tstep + hstep));
+          const float2 sv = *reinterpret_cast<const float2*>(sb + i * kStep * 16);
           float part[MG][4];
           if constexpr (EXACT) {
             // the reference's weights (level x scale, rounded), multiplied
@@ -848,7 +864,6 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * slot);  // this warp is done with the slot
-      if (++cslot == (uint32_t)S) cslot = 0, cphase ^= 1u;
     }
 
     consumer_sync();  // every warp is done with the ring (the partial sums may reuse it)
@@ -857,15 +872,16 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     if (stop) break;
     float* red = q.red_off ? reinterpret_cast<float*>(smem + q.red_off) : reinterpret_cast<float*>(smem + (ring - sbase));
     float4* red4 = reinterpret_cast<float4*>(red);
-    // partial sums [block column][tile][group][fragment]: the two warps of a
-    // column fill disjoint tiles
+    // partial sums [part][tile][group][fragment]: stage split, part = warp
+    // (every warp holds every tile); tile split, part = block column (the
+    // two warps of a column fill disjoint tiles)
 #pragma unroll
     for (int i = 0; i < NTW; ++i) {
-      const int nt = th + kNfSplit * i;
-      if (NT % kNfSplit != 0 && nt >= NT) break;
+      const int nt = SS ? i : th + kNfSplit * i;
+      if (!SS && NT % kNfSplit != 0 && nt >= NT) break;
 #pragma unroll
       for (int gr = 0; gr < MG; ++gr)
-        red4[((bw * NT + nt) * MG + gr) * 32 + lane] =
+        red4[(((SS ? warp : bw) * NT + nt) * MG + gr) * 32 + lane] =
             make_float4(acc[i][gr][0], acc[i][gr][1], acc[i][gr][2], acc[i][gr][3]);
     }
     if (ch == 0) {
@@ -902,7 +918,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       if (nt >= ntl || rl >= R || m >= M) continue;
       float sum = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kStageBlocks; ++w) sum += red[w * (NT * MG * 128) + e];
+      for (int w = 0; w < (SS ? kNfWarps : kStageBlocks); ++w) sum += red[w * (NT * MG * 128) + e];
       const int row = c0 + rl;
       float uu = 0.0f;
       if (has_lora) {
@@ -1098,7 +1114,7 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r, bool exact)
   off += align16((size_t)pl->nt * 16 * (r > 0 ? r : 0) * 2);
   pl->ring_off = (uint32_t)off;
   off += 1024;  // room to round the ring up to a 1 KB shared address
-  const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)kStageBlocks * pl->nt * pl->mg * 512;
+  const size_t ring = (size_t)pl->slots * pl->slot_bytes, red = (size_t)(nf4_stage_split(pl->mg, pl->nt) ? kNfWarps : kStageBlocks) * pl->nt * pl->mg * 512;
   if (pl->chunks == 1) {
     pl->red_off = 0;
     pl->smem = off + (ring > red ? ring : red);
@@ -1171,9 +1187,9 @@ bool gemv_nf4_fits(const QWeight& w, int64_t M, int r) {
          nf4_plan(w.N, w.K, M, r, nf4_esz(w), false, exact, &pl) && nf4_plan(w.N, w.K, M, r, nf4_esz(w), true, exact, &pl);
 }
 
-template <int DT, int MG, int NT, bool EXACT>
-static int nf4_launch(const Nf4Args& q, size_t smem, cudaStream_t st) {
-  auto kern = gemv_nf4_k<DT, MG, NT, EXACT>;
+template <int DT, int MG, int NT, bool EXACT, bool SS>
+static int nf4_launch1(const Nf4Args& q, size_t smem, cudaStream_t st) {
+  auto kern = gemv_nf4_k<DT, MG, NT, EXACT, SS>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -1192,6 +1208,13 @@ static int nf4_launch(const Nf4Args& q, size_t smem, cudaStream_t st) {
     return RQ_ERR_CUDA;
   }
   return check_launch();
+}
+
+template <int DT, int MG, int NT, bool EXACT>
+static int nf4_launch(const Nf4Args& q, size_t smem, cudaStream_t st) {
+  if constexpr (nf4_stage_split(MG, NT))
+    if (q.stage_split) return nf4_launch1<DT, MG, NT, EXACT, true>(q, smem, st);
+  return nf4_launch1<DT, MG, NT, EXACT, false>(q, smem, st);
 }
 
 template <int DT, int MG, bool EXACT>
@@ -1253,6 +1276,9 @@ int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st) {
   q.stg_off = pl.stg_off;
   q.bsm_off = pl.bsm_off;
   q.bsm = pl.chunks == 1 && g.r > 0 && g.r % 8 == 0 && ((uintptr_t)g.lora_b % 16) == 0;
+  // the stage split keeps two stages in consumption at once: only with a
+  // ring of 4 or more stages (else nothing would stream meanwhile)
+  q.stage_split = nf4_stage_split(pl.mg, pl.nt) && pl.slots >= 4;
   // behind a separate down-product kernel X is complete at launch; with the
   // down product fused, the grid before may still be writing X
   q.xsafe = g.r > 0 && !g.fuse_down;
