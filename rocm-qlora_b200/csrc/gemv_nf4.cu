@@ -212,6 +212,7 @@ struct Nf4Args {
                      // down-product kernel, which lets it launch only after
                      // its own griddepcontrol.wait), so X is loaded at once
   int slots;         // ring stages S
+  int sw;            // stages a scale window (0: the pass's scales decoded at once)
   uint32_t slot_bytes;  // 2 * NT*16*128 (codes) + M*1024 (X), a multiple of 1024
   uint32_t ring_off;    // dynamic offsets: ring (rounded up to 1024 in the shared window),
   uint32_t red_off;     //   partial sums (0: the ring itself),
@@ -516,7 +517,37 @@ __host__ __device__ __forceinline__ int mma_row(int g, int wide) { return wide ?
 // MMA row of tile row rr (0..15) modulo 8
 __host__ __device__ __forceinline__ int mma_of_row(int rr, int wide) { return wide ? (rr & 7) : ((rr & 7) >> 1) + 4 * (rr & 1); }
 
-template <int DT, int MG, int NT, bool EXACT, bool SS>
+// The block scales of blocks [b0, b0 + W) of a pass's R rows (first row c0)
+// into the staged table sc (block b0 at sc row 0), for passes whose table
+// is decoded window by window: from the raw bytes in shared memory (the
+// tail under 16 bytes from global memory), the second level through the
+// fp8 / int8 table times c2_scales.
+__device__ __noinline__ void nf4_decode_window(const GemvArgs& p, int wide, int nbk, int esz, int sp, int c0, int R,
+                                               int b0, int W, uint32_t inraw, const unsigned char* raw,
+                                               const float* sclut, const float* c2s_sm, float* sc) {
+  const int tid = threadIdx.x, fmt = p.w.fmt;
+  const int64_t f0 = (int64_t)c0 * nbk;
+  const int total = R * W, f0lo = (int)(f0 & 255), dq = kNfThreads / W, dr = kNfThreads - dq * W;
+  int rl = tid / W, bb = tid - rl * W;
+  for (int i = tid; i < total; i += kNfThreads) {
+    const int e = rl * nbk + b0 + bb;  // entry of the pass
+    float v;
+    if (fmt == RQ_W_NF4) {
+      if ((uint32_t)e < inraw) v = esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e);
+      else v = load_scalar(p.w.scales, p.w.sdt, f0 + e);
+    } else {
+      const uint32_t code = (uint32_t)e < inraw ? (uint32_t)raw[e] : (uint32_t)__ldg(p.w.c2 + f0 + e);
+      v = sclut[code] * c2s_sm[(f0lo + e) >> 8];
+    }
+    const int rr = rl & 15, gg = mma_of_row(rr, wide);
+    sc[bb * sp + (rl >> 4) * 16 + gg * 2 + (rr >> 3)] = v;
+    bb += dr;
+    rl += dq;
+    if (bb >= W) bb -= W, ++rl;
+  }
+}
+
+template <int DT, int MG, int NT, bool EXACT, bool SS, bool WIN>
 __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_constant__ Nf4Args q) {
   using T = typename DType<DT>::T;
   const GemvArgs& p = q.a;
@@ -739,6 +770,8 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     }
   };
 
+  const int swin = q.sw;  // 0: whole pass
+
   int t0, t1;
   pass_tiles(0, t0, t1);
   if (t1 > t0) c2s_load(t0 * 16, (t1 * 16 < N ? t1 * 16 : N) - t0 * 16);
@@ -780,7 +813,11 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // the pass's raw scales have landed: decode them, then hand the buffer back
     mbar_wait(scfull, ch & 1, abortp);
     ++passes;
-    decode(c0, R);
+    if constexpr (WIN)
+      nf4_decode_window(p, q.wide, nbk, esz, sp, c0, R, 0, swin * kStageBlocks < nbk ? swin * kStageBlocks : nbk,
+                        raw_bytes(R) / esz, raw, sclut, c2s_sm, sc);
+    else
+      decode(c0, R);
     consumer_sync();
     if (tid == 0) mbar_arrive(scempty);
 
@@ -798,7 +835,10 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     const float* scw = sc + bw * sp + (SS ? 0 : th * 16) + g * 2;
     const uint32_t cofs_w = cofs + (SS ? 0u : th * tstep);
 
-    for (int s = 0; s < nst; ++s, ++u) {
+    // stages [s_begin, s_end) against the scale table of the window that
+    // starts at stage s0
+    auto run_stages = [&](int s_begin, int s_end, int s0) {
+    for (int s = s_begin; s < s_end; ++s, ++u) {
       const uint32_t slot = cslot, par = cphase;
       if (++cslot == (uint32_t)S) cslot = 0, cphase ^= 1u;
       if (SS && (s & (kNfSplit - 1)) != th) continue;
@@ -815,7 +855,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           x[gr][0] = u0.x, x[gr][1] = u0.y, x[gr][2] = u0.z, x[gr][3] = u0.w;
           x[gr][4] = u1.x, x[gr][5] = u1.y, x[gr][6] = u1.z, x[gr][7] = u1.w;
         }
-        const float* sb = scw + (size_t)s * kStageBlocks * sp;
+        const float* sb = scw + (size_t)(s - s0) * kStageBlocks * sp;
 #pragma unroll
         for (int i = 0; i < NTW; ++i) {
           constexpr int kStep = SS ? 1 : kNfSplit;  // tile stride of this warp's tiles
@@ -864,6 +904,23 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * slot);  // this warp is done with the slot
+    }
+    };
+    if constexpr (WIN) {
+      for (int s0 = 0; s0 < nst; s0 += swin) {
+        if (s0 > 0) {
+          // next scale window: every warp is done with the stages before s0
+          consumer_sync();
+          const int b0 = s0 * kStageBlocks;
+          nf4_decode_window(p, q.wide, nbk, esz, sp, c0, R, b0,
+                            nbk - b0 < swin * kStageBlocks ? nbk - b0 : swin * kStageBlocks, raw_bytes(R) / esz, raw,
+                            sclut, c2s_sm, sc);
+          consumer_sync();
+        }
+        run_stages(s0, s0 + swin < nst ? s0 + swin : nst, s0);
+      }
+    } else {
+      run_stages(0, nst, 0);
     }
 
     consumer_sync();  // every warp is done with the ring (the partial sums may reuse it)
@@ -1089,7 +1146,7 @@ int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64
 }
 
 struct Nf4Plan {
-  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots;
+  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots, sw;
   size_t smem;
   uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
 };
@@ -1101,7 +1158,8 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r, bool exact)
   pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
   size_t off = lut_bytes(exact);
   pl->sc_off = (uint32_t)off;
-  off += align16((size_t)nbk * pl->sp * 4);
+  const int64_t scb = pl->sw && pl->sw * kStageBlocks < nbk ? pl->sw * kStageBlocks : nbk;  // blocks in sc
+  off += align16((size_t)scb * pl->sp * 4);
   pl->raw_off = (uint32_t)off;
   off += align16((size_t)pl->nt * 16 * nbk * pl->esz) + align16(((size_t)pl->nt * 16 * nbk / 256 + 2) * 4);
   pl->aux_off = (uint32_t)off;
@@ -1143,11 +1201,19 @@ static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool besid
     pl->nt = (int)nt;
     pl->tpc = (int)(nt * ch);
     pl->grid = (int)((tiles + pl->tpc - 1) / pl->tpc);
-    // deepest ring that fits (at least 2 stages)
+    // deepest ring that fits (at least 2 stages) with the pass's whole
+    // scale table; where none fits, with the table decoded 8 stages at a
+    // time rather than more passes (default numerics; measured: windows
+    // cost more than a few extra ring stages gain, but less than a pass)
     pl->sp = (int)(nt * 16 + 2);
-    for (int s = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots); s >= 2; --s) {
-      pl->slots = s;
-      if (nf4_layout(pl, nbk, M, r, exact) <= kNfSmemMax) return true;
+    const int top = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots);
+    for (int sw : {0, 8}) {
+      if (sw && (exact || nst <= sw)) break;
+      pl->sw = sw;
+      for (int s = top; s >= 2; --s) {
+        pl->slots = s;
+        if (nf4_layout(pl, nbk, M, r, exact) <= kNfSmemMax) return true;
+      }
     }
     if (nt == 1) return false;
   }
@@ -1187,9 +1253,9 @@ bool gemv_nf4_fits(const QWeight& w, int64_t M, int r) {
          nf4_plan(w.N, w.K, M, r, nf4_esz(w), false, exact, &pl) && nf4_plan(w.N, w.K, M, r, nf4_esz(w), true, exact, &pl);
 }
 
-template <int DT, int MG, int NT, bool EXACT, bool SS>
+template <int DT, int MG, int NT, bool EXACT, bool SS, bool WIN>
 static int nf4_launch1(const Nf4Args& q, size_t smem, cudaStream_t st) {
-  auto kern = gemv_nf4_k<DT, MG, NT, EXACT, SS>;
+  auto kern = gemv_nf4_k<DT, MG, NT, EXACT, SS, WIN>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -1212,9 +1278,13 @@ static int nf4_launch1(const Nf4Args& q, size_t smem, cudaStream_t st) {
 
 template <int DT, int MG, int NT, bool EXACT>
 static int nf4_launch(const Nf4Args& q, size_t smem, cudaStream_t st) {
+  // scale windows: default numerics, tile split (the plan asks for them
+  // only where the whole-pass table leaves a short ring)
+  if constexpr (!EXACT)
+    if (q.sw) return nf4_launch1<DT, MG, NT, false, false, true>(q, smem, st);
   if constexpr (nf4_stage_split(MG, NT))
-    if (q.stage_split) return nf4_launch1<DT, MG, NT, EXACT, true>(q, smem, st);
-  return nf4_launch1<DT, MG, NT, EXACT, false>(q, smem, st);
+    if (q.stage_split) return nf4_launch1<DT, MG, NT, EXACT, true, false>(q, smem, st);
+  return nf4_launch1<DT, MG, NT, EXACT, false, false>(q, smem, st);
 }
 
 template <int DT, int MG, bool EXACT>
@@ -1266,6 +1336,7 @@ int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st) {
   q.sp = pl.sp;
   q.esz = pl.esz;
   q.slots = pl.slots;
+  q.sw = pl.sw;
   q.slot_bytes = pl.slot_bytes;
   q.ring_off = pl.ring_off;
   q.red_off = pl.red_off;
@@ -1278,7 +1349,7 @@ int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st) {
   q.bsm = pl.chunks == 1 && g.r > 0 && g.r % 8 == 0 && ((uintptr_t)g.lora_b % 16) == 0;
   // the stage split keeps two stages in consumption at once: only with a
   // ring of 4 or more stages (else nothing would stream meanwhile)
-  q.stage_split = nf4_stage_split(pl.mg, pl.nt) && pl.slots >= 4;
+  q.stage_split = nf4_stage_split(pl.mg, pl.nt) && pl.slots >= 4 && pl.sw == 0;
   // behind a separate down-product kernel X is complete at launch; with the
   // down product fused, the grid before may still be writing X
   q.xsafe = g.r > 0 && !g.fuse_down;
