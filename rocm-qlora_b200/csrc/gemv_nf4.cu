@@ -48,8 +48,8 @@
 // this one has finished and its writes are visible: X (without an adapter
 // the producer waits after the first ring fill of codes, then issues X for
 // those stages), x.A^T and the bias (the epilogue), and with the fused
-// gather the flags and counters of the calls before (the whole kernel
-// waits first).  With LoRA the grid before is the layer's down-product
+// gather the flags and counters of the calls before (without an adapter
+// the whole kernel waits first).  With LoRA the grid before is the layer's down-product
 // kernel; it lets this one launch only after its own griddepcontrol.wait,
 // so X is complete at launch and is streamed with the codes from the first
 // stage, while the down product runs beside the main loop.
@@ -561,8 +561,10 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   // it reads anything but weights.
   asm volatile("griddepcontrol.launch_dependents;");
   // The gather's flags and counters are written by the calls before this
-  // one: a gather kernel waits for the grids before it at once.
-  if (q.a.gather) asm volatile("griddepcontrol.wait;" ::: "memory");
+  // one: a gather kernel waits for the grids before it at once -- unless it
+  // follows the down-product kernel (xsafe), which let it launch only after
+  // its own wait, when those calls had finished.
+  if (q.a.gather && !q.xsafe) asm volatile("griddepcontrol.wait;" ::: "memory");
   // fused LoRA down product: the grid's first kNfDownCtas CTAs
   if (p.fuse_down && blockIdx.x < (unsigned)kNfDownCtas) {
     if (p.r <= 16) down_role<DT, 2>(p, smem);

@@ -78,6 +78,18 @@ def _check_device(w: WeightView, x: torch.Tensor) -> None:
 _ws_bytes = {}  # rq_linear_workspace_bytes by (M, N, K, r): a pure function of them
 
 
+def _split_adapter(M: int, r: int, dtype: torch.dtype, for_dx: bool) -> bool:
+    """Whether the adapter term runs beside the kernel instead of inside it.
+    The tensor-core GEMM (forward M >= 64, dX every M) takes ranks <= 64
+    that are multiples of 8; other ranks would send those calls to the exact
+    CUDA-core kernel (slow at these sizes).  They run the kernel without
+    the adapter and add the adapter term with cuBLAS matmuls in the
+    activation dtype, rounding as the reference does."""
+    if r == 0 or (r <= 64 and r % 8 == 0) or dtype not in (torch.bfloat16, torch.float16):
+        return False
+    return for_dx or M >= 64
+
+
 def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: Optional[torch.Tensor],
             B: Optional[torch.Tensor], scaling: float, lora_x: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y[M, N] of LoRALinear.forward (eval) over QuantLinear.forward."""
@@ -87,6 +99,11 @@ def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: O
     M = x2d.shape[0]
     dt = nat.dtype_code(x2d.dtype)
     r = 0 if A is None else A.shape[0]
+    if _split_adapter(M, r, x2d.dtype, False):
+        # rnd(base + rnd(rnd(rnd(x_l . A^T) . B^T) * s)), base = rnd(x . W^T (+ bias))
+        base = forward(w, x2d, bias, None, None, 1.0)
+        xin = lora_x if lora_x is not None else x2d
+        return base + (xin @ A.t()) @ B.t() * scaling
     y = torch.empty(M, w.N, dtype=x2d.dtype, device=dev)
     key = (M, w.N, w.K, r)
     nbytes = _ws_bytes.get(key)
@@ -203,6 +220,8 @@ def dx(w: WeightView, dy2d: torch.Tensor, A: Optional[torch.Tensor], B: Optional
     dev = dy2d.device
     M = dy2d.shape[0]
     r = 0 if A is None else A.shape[0]
+    if _split_adapter(M, r, dy2d.dtype, True):
+        return dx(w, dy2d, None, None, 1.0) + ((dy2d * scaling) @ B) @ A
     out = torch.empty(M, w.K, dtype=dy2d.dtype, device=dev)
     with torch.cuda.device(dev):
         nbytes = L.rq_linear_workspace_bytes(M, w.N, w.K, r)

@@ -372,3 +372,20 @@ def test_decode_fused_down_product(r, M):
     with torch.cuda.stream(s):
         ws_s = nat.workspace(torch.device("cuda", torch.cuda.current_device()), 0)
     assert int(ws_s[:256].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("r,M", [(12, 64), (72, 300), (128, 40), (128, 256)])
+def test_prefill_ranks_beside_the_gemm(r, M):
+    """Ranks the tensor-core GEMM does not take (r > 64, r % 8 != 0) at
+    prefill / training sizes: the kernel runs without the adapter and the
+    adapter term is added with matmuls in the activation dtype; forward and
+    dX keep the reference's roundings."""
+    N, K = 512, 1024
+    inp = layer_inputs(N, K, M, sigma=0.03, r=r, alpha=2 * r, seed=900 + r + M, with_dy=True)
+    lora = build_layer(inp.W, 4, True, None, inp.r, inp.alpha, inp.A, inp.B)
+    x = inp.X.cuda().requires_grad_(True)
+    y = lora(x)
+    y.backward(inp.dY.cuda())
+    y_ref, dx_ref = _oracle_y_dx(lora, inp.X, inp.dY)
+    assert_matmul_close(to_f32(y), y_ref, 1, label=f"rank {r} M{M} forward")
+    assert_matmul_close(to_f32(x.grad), dx_ref, 1, label=f"rank {r} M{M} dx")
