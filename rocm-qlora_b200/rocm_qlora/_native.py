@@ -20,7 +20,10 @@ from typing import Dict, Optional, Tuple
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.environ.get("RQ_B200_LIB", os.path.join(_HERE, "librqb200.so"))
+_DEFAULT_LIB = os.path.join(_HERE, "librqb200.so")
+LIB_PATH = os.environ.get("RQ_B200_LIB", _DEFAULT_LIB)
+# the thin torch extension over the same library (csrc/torch_ops.cpp)
+OPS_PATH = os.path.join(_HERE, "librq_torch_ops.so")
 
 RQ_OK = 0
 RQ_ERR_UNSUPPORTED = -8
@@ -117,6 +120,29 @@ def load_library() -> ctypes.CDLL:
             _bind(L)
             _lib = L
     return _lib
+
+
+_ops_state: Optional[bool] = None
+
+
+def ops() -> bool:
+    """Whether torch.ops.rocm_qlora.{linear_forward, linear_dx} are loaded:
+    the layer then calls the library through one dispatcher call instead of
+    ctypes.  Only with the in-tree library (the extension links it), so a
+    library chosen through RQ_B200_LIB is always called directly."""
+    global _ops_state
+    if _ops_state is None:
+        with _lib_lock:
+            if _ops_state is None:
+                ok = False
+                if os.path.abspath(LIB_PATH) == _DEFAULT_LIB and os.path.exists(OPS_PATH):
+                    try:
+                        torch.ops.load_library(OPS_PATH)
+                        ok = hasattr(torch.ops.rocm_qlora, "linear_forward")
+                    except (OSError, RuntimeError):
+                        ok = False
+                _ops_state = ok
+    return _ops_state
 
 
 def device_supported(device: Optional[torch.device] = None) -> bool:

@@ -2,7 +2,9 @@
 
 ``QuantLinear.forward`` and ``LoRALinear.forward`` call into here; each call
 is one ``rq_linear_forward`` (and, in backward, one ``rq_linear_dx``) on the
-current CUDA stream.  The adapter gradients dA / dB are plain cuBLAS matmuls
+current CUDA stream, through the torch extension's operators
+(``torch.ops.rocm_qlora.linear_forward`` / ``linear_dx``, csrc/torch_ops.cpp)
+or, where that extension is not built, through ctypes.  The adapter gradients dA / dB are plain cuBLAS matmuls
 in the activation dtype with the same roundings as the reference's autograd
 of ``x @ A.T @ B.T * scaling`` (rocm_qlora/lora/lora_layer.py:67).
 """
@@ -104,11 +106,18 @@ def forward(w: WeightView, x2d: torch.Tensor, bias: Optional[torch.Tensor], A: O
         base = forward(w, x2d, bias, None, None, 1.0)
         xin = lora_x if lora_x is not None else x2d
         return base + (xin @ A.t()) @ B.t() * scaling
-    y = torch.empty(M, w.N, dtype=x2d.dtype, device=dev)
     key = (M, w.N, w.K, r)
     nbytes = _ws_bytes.get(key)
     if nbytes is None:
         nbytes = _ws_bytes[key] = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
+
+    if nat.ops():
+        # one dispatcher call: device guard, output, x's device's current
+        # stream and the status check are in the extension
+        return torch.ops.rocm_qlora.linear_forward(
+            x2d, w.fmt, w.q, w.scales, w.c2, w.c2_scales, w.N, w.K, w.block_size, lora_x, bias, A, B,
+            float(scaling), nat.workspace(dev, nbytes))
+    y = torch.empty(M, w.N, dtype=x2d.dtype, device=dev)
 
     def call():
         st = nat.stream_ptr(dev)
@@ -222,10 +231,13 @@ def dx(w: WeightView, dy2d: torch.Tensor, A: Optional[torch.Tensor], B: Optional
     r = 0 if A is None else A.shape[0]
     if _split_adapter(M, r, dy2d.dtype, True):
         return dx(w, dy2d, None, None, 1.0) + ((dy2d * scaling) @ B) @ A
-    out = torch.empty(M, w.K, dtype=dy2d.dtype, device=dev)
     with torch.cuda.device(dev):
         nbytes = L.rq_linear_workspace_bytes(M, w.N, w.K, r)
         ws = nat.workspace(dev, nbytes)
+        if nat.ops():
+            return torch.ops.rocm_qlora.linear_dx(dy2d, w.fmt, w.q, w.scales, w.c2, w.c2_scales, w.N, w.K,
+                                                  w.block_size, A, B, float(scaling), ws)
+        out = torch.empty(M, w.K, dtype=dy2d.dtype, device=dev)
         nat.check(L.rq_linear_dx(*w.args(), dy2d.data_ptr(), nat.dtype_code(dy2d.dtype), M, nat.ptr(A), nat.ptr(B),
                                  r, float(scaling), out.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
                   "rq_linear_dx")

@@ -389,3 +389,30 @@ def test_prefill_ranks_beside_the_gemm(r, M):
     y_ref, dx_ref = _oracle_y_dx(lora, inp.X, inp.dY)
     assert_matmul_close(to_f32(y), y_ref, 1, label=f"rank {r} M{M} forward")
     assert_matmul_close(to_f32(x.grad), dx_ref, 1, label=f"rank {r} M{M} dx")
+
+
+@pytest.mark.parametrize("M,r", [(4, 16), (300, 64), (96, 0)])
+def test_torch_ops_equal_ctypes_calls(M, r):
+    """torch.ops.rocm_qlora.* (the extension) and direct ctypes calls of the
+    C ABI launch the same kernels: identical forward and dX bytes."""
+    from rocm_qlora import _native as nat
+    N, K = 640, 2048
+    inp = layer_inputs(N, K, M, sigma=0.03, r=max(r, 1), alpha=32, seed=1200 + M + r, with_dy=True)
+    lora = build_layer(inp.W, 4, True, None, inp.r, inp.alpha, inp.A, inp.B)
+    assert nat.ops()
+
+    def run():
+        x = inp.X.cuda().requires_grad_(True)
+        y = lora(x) if r else lora.base_layer(x)
+        y.backward(inp.dY.cuda())
+        torch.cuda.synchronize()
+        return y.detach().clone(), x.grad.clone()
+
+    y_ops, dx_ops = run()
+    saved = nat._ops_state
+    try:
+        nat._ops_state = False
+        y_ct, dx_ct = run()
+    finally:
+        nat._ops_state = saved
+    assert torch.equal(y_ops, y_ct) and torch.equal(dx_ops, dx_ct)

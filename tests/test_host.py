@@ -192,3 +192,21 @@ def test_cast_param_cache():
     p.data.zero_()  # not seen by the version counter ...
     lo.forget_casts(p)  # ... hence the explicit reset
     assert float(lo.cast_param(p, torch.bfloat16).abs().sum()) == 0
+
+
+def test_torch_extension_registers_the_layer_ops():
+    """The thin torch extension over the C ABI (librq_torch_ops.so) loads
+    without a GPU and registers both layer operators; their Meta kernels
+    give the output shapes (tracing)."""
+    import torch
+    from rocm_qlora import _native as nat
+    assert nat.ops(), "librq_torch_ops.so missing or not loadable"
+    ops = torch.ops.rocm_qlora
+    x = torch.empty(5, 128, device="meta", dtype=torch.bfloat16)
+    q = torch.empty(32 * 128 // 2, device="meta", dtype=torch.uint8)
+    ws = torch.empty(256, device="meta", dtype=torch.uint8)
+    y = ops.linear_forward(x, 0, q, None, None, None, 32, 128, 64, None, None, None, None, 1.0, ws)
+    assert y.shape == (5, 32) and y.dtype == torch.bfloat16
+    dy = torch.empty(5, 32, device="meta", dtype=torch.float16)
+    dx = ops.linear_dx(dy, 0, q, None, None, None, 32, 128, 64, None, None, 1.0, ws)
+    assert dx.shape == (5, 128) and dx.dtype == torch.float16
