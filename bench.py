@@ -976,7 +976,7 @@ def run_reference(args, rank, world):
 
 
 def run_case(args, device):
-    """--case decode:N:K:M[:r] or prefill:N:K:M[:r] -- one layer call repeated
+    """--case decode:N:K:M[:r] / decode8:... / decode8row:... (int8 blockwise / per-row) or prefill:N:K:M[:r] -- one layer call repeated
     (for profilers; prints the mean CUDA-event time per call)."""
     import torch.nn as nn
     from rocm_qlora import LoRALinear, QuantLinear
@@ -1011,8 +1011,15 @@ def run_case(args, device):
     lin = nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=device)
     with torch.no_grad():
         lin.weight.copy_(inp.W.to(device))
-    ql = QuantLinear.from_linear(lin, bits=4)
-    ql.enable_double_quant()
+    if kind in ("decode8", "decode8row"):  # int8 blockwise / per-row weights
+        ql = QuantLinear(K, N, bits=8, bias=False).to(device)
+        from rocm_qlora.quantization import quantize_int8
+        wq, ws_ = quantize_int8(lin.weight.detach(), per_channel=kind == "decode8row")
+        ql.weight_quant, ql.weight_scales = wq, ws_
+        kind = "decode"
+    else:
+        ql = QuantLinear.from_linear(lin, bits=4)
+        ql.enable_double_quant()
     lora = LoRALinear(ql, r=max(r, 1), lora_alpha=2 * max(r, 1)).to(device).eval()
     with torch.no_grad():
         lora.lora_A.copy_(inp.A)

@@ -301,11 +301,13 @@ static void gemv_shape(int wk, int64_t N, int64_t K, int64_t M, int r, int* grid
   *nt = (int)n;
 }
 
-// Whether the NF4 GEMV can compute the layer's LoRA down product in its own
-// grid (gemv_nf4.cu, down_role): an adapter of rank <= 64, no fused gather,
+// Whether the TMA-ring GEMV (gemv_nf4.cu: NF4 formats, int8 with K % 128 == 0)
+// can compute the layer's LoRA down product in its own grid (down_role): an
+// adapter of rank <= 64, no fused gather,
 // 4-byte aligned x_lora rows and A rows (K is a multiple of 64).
 bool gemv_fuse_down(const LinearArgs& a) {
-  return is_nf4_fmt(a.w.fmt) && a.r > 0 && a.r <= 64 && a.M >= 1 && a.M <= 16 && a.gather == nullptr &&
+  const bool ring = is_nf4_fmt(a.w.fmt) || gemv_nf4_fits(a.w, a.M, a.r);  // the TMA-ring kernel runs the call
+  return ring && a.r > 0 && a.r <= 64 && a.M >= 1 && a.M <= 16 && a.gather == nullptr &&
          a.lora_x != nullptr && a.lora_a != nullptr && ((uintptr_t)a.lora_x % 4) == 0 &&
          ((uintptr_t)a.lora_a % 4) == 0;
 }
@@ -317,6 +319,7 @@ bool gemv_supported(const LinearArgs& a) {
   if ((uintptr_t)a.x % 16 || (uintptr_t)a.w.q % 16) return false;
   if (a.w.N > 0x7fffffff || a.w.K > 0x7fffffff || (a.w.N * a.w.K) / 2 > 0xfffffff0ll) return false;
   if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_fits(a.w, a.M, a.r);
+  if (gemv_nf4_fits(a.w, a.M, a.r)) return true;  // int8 on the TMA-ring kernel
   const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;
   return smem_for(wk, a.w.K, 1, a.M, a.r) <= kGemvSmemCap;
 }
@@ -379,7 +382,9 @@ int gemv_forward(const LinearArgs& a, const void* tdown, cudaStream_t st, float*
   g.partial = partial;
   g.counters = counters;
   if (is_nf4_fmt(a.w.fmt)) return gemv_nf4_forward(g, a.r > 0, st);
-  if (a.gather) return RQ_ERR_UNSUPPORTED;  // the INT8 kernel has no gather epilogue
+  if (a.gather) return RQ_ERR_UNSUPPORTED;  // int8: no fused gather
+  // int8 rows that travel as 128-byte pieces: the TMA-ring kernel (gemv_nf4.cu)
+  if (gemv_nf4_fits(a.w, a.M, a.r)) return gemv_nf4_forward(g, a.r > 0, st);
   const int wk = a.w.fmt == RQ_W_INT8 ? 1 : 2;
   int nt = 1;
   gemv_shape(wk, a.w.N, a.w.K, a.M, a.r, &g.grid, &g.tiles, &g.chunks, &nt);

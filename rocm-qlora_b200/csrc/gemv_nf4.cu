@@ -208,6 +208,7 @@ struct Nf4Args {
   int esz;           // bytes per raw scale (1: c2 codes; 2/4: plain scales)
   int wide;          // 1: 3-D code box (K % 256 == 0)
   int stage_split;   // 1: the two warps of a block column split the stages (nf4_stage_split)
+  int wk;            // code format: 0 NF4 family, 1 int8 blockwise, 2 int8 per-row
   int xsafe;         // 1: X is complete when this grid launches (it follows the
                      // down-product kernel, which lets it launch only after
                      // its own griddepcontrol.wait), so X is loaded at once
@@ -499,6 +500,18 @@ __device__ __forceinline__ uint32_t ref_pair(uint2 lv, float s) {
   return d;
 }
 
+// int8 codes B and B+1 of `w` as a 16-bit pair (exact: |code| <= 128)
+template <int DT, int B>
+__device__ __forceinline__ uint32_t i8pair(uint32_t w) {
+  const float f0 = (float)(int8_t)(w >> (8 * B)), f1 = (float)(int8_t)(w >> (8 * B + 8));
+  uint32_t d;
+  if constexpr (DT == RQ_BF16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f1), "f"(f0));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f1), "f"(f0));
+  return d;
+}
+
 template <int DT, int MG>
 __device__ __forceinline__ void kstep(float (&part)[MG][4], bool first, uint32_t a0, uint32_t a1, uint32_t a2,
                                       uint32_t a3, const uint32_t (&x)[MG][8], int j) {
@@ -547,7 +560,7 @@ __device__ __noinline__ void nf4_decode_window(const GemvArgs& p, int wide, int 
   }
 }
 
-template <int DT, int MG, int NT, bool EXACT, bool SS, bool WIN>
+template <int DT, int MG, int NT, bool EXACT, bool SS, bool WIN, int WK>
 __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_constant__ Nf4Args q) {
   using T = typename DType<DT>::T;
   const GemvArgs& p = q.a;
@@ -581,12 +594,15 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   const int sp = q.sp, S = q.slots;
   const uint32_t slot_bytes = q.slot_bytes;
   constexpr uint32_t kBox = NT * 16 * 128;  // one 128-byte-wide code box
+  // code boxes of a stage (NF4: 256 bytes a row, int8: 512) and X after them
+  constexpr uint32_t kCodeBoxes = WK ? 4u : 2u, kXOff = kCodeBoxes * kBox;
   const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(bars), empty0 = full0 + kNfMaxSlots * 8;
   const uint32_t scfull = full0 + 2 * kNfMaxSlots * 8, scempty = scfull + 8;
   // raw scale bytes of the pass at rows [c0, c0+R): one copy of the 16-byte
   // aligned part (the rest, under 16 bytes, is read directly)
   const int esz = q.esz;
-  const unsigned char* rawsrc = static_cast<const unsigned char*>(p.w.fmt == RQ_W_NF4 ? p.w.scales : (const void*)p.w.c2);
+  const unsigned char* rawsrc = static_cast<const unsigned char*>(
+      p.w.fmt == RQ_W_NF4 || p.w.fmt == RQ_W_INT8 ? p.w.scales : (const void*)p.w.c2);
   auto raw_bytes = [&](int R) { return (uint32_t)(R * nbk * esz) & ~15u; };
   volatile int* abortp = &abort_flag;
   volatile int* issuedp = &issued;
@@ -630,14 +646,14 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // only, and X of those stages follows once the grids before this one
     // have finished (griddepcontrol.wait; gather kernels waited at start).
     if (lane == 0) {
-      const uint32_t bytes = 2 * kBox + (uint32_t)M * 1024;
+      const uint32_t bytes = kXOff + (uint32_t)M * 1024;
       uint32_t u = 0, xpend = 0;  // stages 0 .. xpend-1 of pass 0 still wait for X
       bool xopen = p.gather != 0 || q.xsafe != 0;
       const uint32_t fill = (uint32_t)(nst < S ? nst : S);
       auto open_x = [&]() {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         for (uint32_t v = 0; v < xpend; ++v)
-          tma_load_2d(ring + v * slot_bytes + 2 * kBox, &q.xmap, (int)v * 256, 0, full0 + 8 * v);
+          tma_load_2d(ring + v * slot_bytes + kXOff, &q.xmap, (int)v * 256, 0, full0 + 8 * v);
         xpend = 0;
         xopen = true;
       };
@@ -665,14 +681,16 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
           if (u >= (uint32_t)S && !mbar_wait(empty0 + 8 * slot, ((u / S) - 1) & 1, abortp)) break;
           const uint32_t dst = ring + slot * slot_bytes, bar = full0 + 8 * slot;
           mbar_expect_tx(bar, bytes);
-          if (q.wide) {
+          if (WK) {  // int8: [rows][4][128 B], 512 bytes a row
+            tma_load_3d(dst, &q.wmap, 0, 4 * s, t0 * 16, bar);
+          } else if (q.wide) {
             tma_load_3d(dst, &q.wmap, 0, 2 * s, t0 * 16, bar);
           } else {
             tma_load_2d(dst, &q.wmap, s * 256, t0 * 16, bar);
             tma_load_2d(dst + kBox, &q.wmap, s * 256 + 128, t0 * 16, bar);
           }
           if (xopen) {
-            tma_load_2d(dst + 2 * kBox, &q.xmap, s * 256, 0, bar);
+            tma_load_2d(dst + kXOff, &q.xmap, s * 256, 0, bar);
           } else {
             ++xpend;  // pass 0, stage s == u in slot u
             if (xpend == fill) open_x();
@@ -707,20 +725,24 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   // the 128-byte shared rows are swizzled by their index mod 8.
   //   3-D: shared row 2*r + half -> per tile 4096 bytes, per h 2048
   //   2-D: half at kBox, shared row r -> per tile 2048 bytes, per h 1024
-  const int wide = q.wide;
+  //   int8: the lane's 16 bytes of block bw are 16-byte chunk 4*(bw & 1) + t of
+  //   quarter bw >> 1 of the tile row; shared row 4*r + quarter -> per tile
+  //   8192 bytes, per h 4096
+  const int wide = WK ? 1 : q.wide;
   const int pg = mma_row(g, wide), half = bw >> 2, lch = 2 * (bw & 3) + (t >> 1);
-  // (a tile is 16 or 32 shared rows: the swizzle phase repeats per tile)
-  const uint32_t tstep = wide ? 4096u : 2048u, hstep = tstep / 2;
+  // (a tile is 16, 32 or 64 shared rows: the swizzle phase repeats per tile)
+  const uint32_t tstep = WK ? 8192u : (wide ? 4096u : 2048u), hstep = tstep / 2;
   const uint32_t cofs =
-      (wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
-                         : (uint32_t)half * kBox + pg * 128 + (((lch ^ pg) << 4) | ((t & 1) << 3)));
+      WK ? (uint32_t)(4 * pg + (bw >> 1)) * 128 + ((((bw & 1) * 4 + t) ^ ((4 * pg + (bw >> 1)) & 7)) << 4)
+         : (wide ? (uint32_t)(2 * pg + half) * 128 + (((lch ^ (2 * (pg & 3) + half)) << 4) | ((t & 1) << 3))
+                 : (uint32_t)half * kBox + pg * 128 + (((lch ^ pg) << 4) | ((t & 1) << 3)));
   // lane's X in a slot: token gr*8 + g (tokens past M read token M-1, results
   // dropped), columns of block bw, 16 t .. 16 t + 15
   uint32_t xofs[MG];
 #pragma unroll
   for (int gr = 0; gr < MG; ++gr) {
     const int m = gr * 8 + g;
-    xofs[gr] = 2 * kBox + (uint32_t)(m < M ? m : M - 1) * 1024 + bw * 128 + t * 32;
+    xofs[gr] = kXOff + (uint32_t)(m < M ? m : M - 1) * 1024 + bw * 128 + t * 32;
   }
 
   // decoded scales of the pass at rows [c0, c0+R) into sc in fragment order
@@ -729,7 +751,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   const unsigned char* raw = smem + q.raw_off;
   float* c2s_sm = reinterpret_cast<float*>(smem + q.raw_off + ((NT * 16 * nbk * esz + 15) & ~15));
   auto c2s_load = [&](int c0, int R) {  // the pass's c2_scales (one per 256 blocks)
-    if (fmt == RQ_W_NF4) return;
+    if (fmt == RQ_W_NF4 || WK) return;
     const int64_t f0 = (int64_t)c0 * nbk;
     const int n = (int)(((f0 + (int64_t)R * nbk - 1) >> 8) - (f0 >> 8)) + 1;
     for (int i = tid; i < n; i += kNfThreads) c2s_sm[i] = __ldg(p.w.c2s + (f0 >> 8) + i);
@@ -753,7 +775,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     // global memory: separate loops, so that no shared entry waits on a
     // global load the compiler would otherwise issue for every entry
     int e = tid;
-    if (fmt == RQ_W_NF4) {
+    if (fmt == RQ_W_NF4 || fmt == RQ_W_INT8) {
       for (; e < inraw; e += kNfThreads)
         put(esz == 4 ? reinterpret_cast<const float*>(raw)[e] : load_scalar(raw, p.w.sdt, e));
       for (; e < total; e += kNfThreads) put(load_scalar(p.w.scales, p.w.sdt, f0 + e));
@@ -779,7 +801,9 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
   if (t1 > t0) c2s_load(t0 * 16, (t1 * 16 < N ? t1 * 16 : N) - t0 * 16);
   // code table (entry v: 32 copies of the pair (T[v & 15], T[v >> 4])) and
   // the second-level table, built while the first stages are in flight
-  if constexpr (EXACT) {
+  // (int8 codes need neither)
+  if constexpr (WK) {
+  } else if constexpr (EXACT) {
     // entry v: 32 copies of the fp32 pair (T[v & 15], T[v >> 4]), 8 bytes a lane
     const float lvl = nf4_level_imm(lane & 15);
 #pragma unroll 1
@@ -798,7 +822,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
       *reinterpret_cast<uint4*>(lut + v * 128 + (tid & 7) * 16) = make_uint4(w, w, w, w);
     }
   }
-  if (fmt != RQ_W_NF4 && tid < 256)
+  if (!WK && fmt != RQ_W_NF4 && tid < 256)
     sclut[tid] = fmt == RQ_W_NF4_DQ_FP8 ? e4m3fnuz_to_f32(tid) : ieee_div((float)(int8_t)tid, 127.0f);
 
   start_wait();  // the producer's mbarriers and flags are initialized
@@ -818,7 +842,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
     if constexpr (WIN)
       nf4_decode_window(p, q.wide, nbk, esz, sp, c0, R, 0, swin * kStageBlocks < nbk ? swin * kStageBlocks : nbk,
                         raw_bytes(R) / esz, raw, sclut, c2s_sm, sc);
-    else
+    else if constexpr (WK != 2)  // int8 per-row scales apply in the epilogue
       decode(c0, R);
     consumer_sync();
     if (tid == 0) mbar_arrive(scempty);
@@ -862,6 +886,43 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
         for (int i = 0; i < NTW; ++i) {
           constexpr int kStep = SS ? 1 : kNfSplit;  // tile stride of this warp's tiles
           if (!SS && NT % kNfSplit != 0 && th + kNfSplit * i >= NT) break;
+          if constexpr (WK != 0) {
+            // int8: 16 codes of row g and of row g+8; word j holds the codes
+            // of k-step j (k 4j .. 4j+3 of the lane's 16, as X is laid out)
+            uint4 l4, h4;
+            asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(l4.x), "=r"(l4.y), "=r"(l4.z), "=r"(l4.w)
+                         : "r"(sl + cofs_w + i * kStep * tstep));
+            asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(h4.x), "=r"(h4.y), "=r"(h4.z), "=r"(h4.w)
+                         : "r"(sl + cofs_w + i * kStep * tstep + hstep));
+            const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+            if constexpr (WK == 2) {
+              // per-row scales: the codes multiply straight into the
+              // accumulators, the row scale applies in the epilogue
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t a0 = i8pair<DT, 0>(lw[j]), a1 = i8pair<DT, 0>(hw[j]);
+                const uint32_t a2 = i8pair<DT, 2>(lw[j]), a3 = i8pair<DT, 2>(hw[j]);
+#pragma unroll
+                for (int gr = 0; gr < MG; ++gr)
+                  Mma16816<DT>::run(acc[i][gr], a0, a1, a2, a3, x[gr][2 * j], x[gr][2 * j + 1]);
+              }
+            } else {
+              const float2 sv = *reinterpret_cast<const float2*>(sb + i * kStep * 16);
+              float part[MG][4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                kstep<DT, MG>(part, j == 0, i8pair<DT, 0>(lw[j]), i8pair<DT, 0>(hw[j]), i8pair<DT, 2>(lw[j]),
+                              i8pair<DT, 2>(hw[j]), x, j);
+#pragma unroll
+              for (int gr = 0; gr < MG; ++gr) {
+                fma2(acc[i][gr][0], acc[i][gr][1], part[gr][0], part[gr][1], sv.x);
+                fma2(acc[i][gr][2], acc[i][gr][3], part[gr][2], part[gr][3], sv.y);
+              }
+            }
+            continue;
+          }
           uint2 lo, hi;
           asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(lo.x), "=r"(lo.y) : "r"(sl + cofs_w + i * kStep * tstep));
           asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];"
@@ -979,6 +1040,7 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
 #pragma unroll
       for (int w = 0; w < (SS ? kNfWarps : kStageBlocks); ++w) sum += red[w * (NT * MG * 128) + e];
       const int row = c0 + rl;
+      if constexpr (WK == 2) sum *= load_scalar(p.w.scales, p.w.sdt, row);  // int8 per-row scale
       float uu = 0.0f;
       if (has_lora) {
         const T* brow = lb + (size_t)row * p.r;
@@ -1148,7 +1210,7 @@ int tensor_map_encode(int type, int swz, int rank, const void* ptr, const uint64
 }
 
 struct Nf4Plan {
-  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots, sw;
+  int grid, tiles, tpc, chunks, nt, mg, sp, esz, slots, sw, wk;
   size_t smem;
   uint32_t slot_bytes, ring_off, red_off, sc_off, raw_off, aux_off, tl_off, stg_off, bsm_off;
 };
@@ -1157,10 +1219,11 @@ struct Nf4Plan {
 // table | x.A^T | staged outputs | ring (1 KB aligned) | partial sums];
 // with one pass the partial sums reuse the ring.
 static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r, bool exact) {
-  pl->slot_bytes = (uint32_t)(2 * pl->nt * 16 * 128 + M * 1024);
-  size_t off = lut_bytes(exact);
+  pl->slot_bytes = (uint32_t)((pl->wk ? 4 : 2) * pl->nt * 16 * 128 + M * 1024);
+  size_t off = pl->wk ? 0 : lut_bytes(exact);  // int8 codes need no table
   pl->sc_off = (uint32_t)off;
-  const int64_t scb = pl->sw && pl->sw * kStageBlocks < nbk ? pl->sw * kStageBlocks : nbk;  // blocks in sc
+  int64_t scb = pl->sw && pl->sw * kStageBlocks < nbk ? pl->sw * kStageBlocks : nbk;  // blocks in sc
+  if (pl->wk == 2) scb = 0;  // per-row scales
   off += align16((size_t)scb * pl->sp * 4);
   pl->raw_off = (uint32_t)off;
   off += align16((size_t)pl->nt * 16 * nbk * pl->esz) + align16(((size_t)pl->nt * 16 * nbk / 256 + 2) * 4);
@@ -1185,9 +1248,11 @@ static size_t nf4_layout(Nf4Plan* pl, int64_t nbk, int64_t M, int r, bool exact)
   return pl->smem;
 }
 
-static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool beside, bool exact, Nf4Plan* pl) {
+static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, int wk, bool beside, bool exact,
+                     Nf4Plan* pl) {
   pl->mg = M > 8 ? 2 : 1;
   pl->esz = esz;
+  pl->wk = wk;
   const int64_t tiles = (N + 15) / 16;
   // with the down product running beside it, leave the SMs its cluster uses
   int64_t G = num_sms() - (beside ? kLoraDownCtas : 0);
@@ -1210,7 +1275,7 @@ static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool besid
     pl->sp = (int)(nt * 16 + 2);
     const int top = (int)(nst < kNfMaxSlots ? (nst > 2 ? nst : 2) : kNfMaxSlots);
     for (int sw : {0, 8}) {
-      if (sw && (exact || nst <= sw)) break;
+      if (sw && (exact || wk || nst <= sw)) break;  // windows: NF4, default numerics only
       pl->sw = sw;
       for (int s = top; s >= 2; --s) {
         pl->slots = s;
@@ -1221,11 +1286,16 @@ static bool nf4_plan(int64_t N, int64_t K, int64_t M, int r, int esz, bool besid
   }
 }
 
-// bytes per raw scale entry of the weight's format
+// bytes per raw scale entry of the weight's format (0: per-row scales,
+// applied in the epilogue)
 static int nf4_esz(const QWeight& w) {
-  if (w.fmt != RQ_W_NF4) return 1;
-  return w.sdt == RQ_F32 ? 4 : 2;
+  if (w.fmt == RQ_W_INT8_ROW) return 0;
+  if (w.fmt == RQ_W_NF4 || w.fmt == RQ_W_INT8) return w.sdt == RQ_F32 ? 4 : 2;
+  return 1;  // c2 codes
 }
+// kernel code format: 0 NF4 (plain or double-quantized scales), 1 int8
+// blockwise, 2 int8 per-row
+static int nf4_wk(const QWeight& w) { return w.fmt == RQ_W_INT8 ? 1 : (w.fmt == RQ_W_INT8_ROW ? 2 : 0); }
 
 // Decode numerics: 0 = levels rounded once to the activation dtype, the
 // block scale applied to each 64-wide fp32 partial (the default); 1 = the
@@ -1249,15 +1319,20 @@ void set_decode_exact(int on) { g_decode_exact.store(on ? 1 : 0); }
 
 bool gemv_nf4_fits(const QWeight& w, int64_t M, int r) {
   Nf4Plan pl;
-  const void* sp = w.fmt == RQ_W_NF4 ? w.scales : (const void*)w.c2;
-  const bool exact = decode_exact();
-  return encode_tiled() != nullptr && ((uintptr_t)sp % 16) == 0 &&
-         nf4_plan(w.N, w.K, M, r, nf4_esz(w), false, exact, &pl) && nf4_plan(w.N, w.K, M, r, nf4_esz(w), true, exact, &pl);
+  const int wk = nf4_wk(w);
+  // the raw scale copy reads 16-byte aligned sources; int8 rows travel as
+  // 3-D boxes of 128-byte pieces
+  const void* sp = w.fmt == RQ_W_NF4 || w.fmt == RQ_W_INT8 ? w.scales : (const void*)w.c2;
+  if (wk != 2 && ((uintptr_t)sp % 16) != 0) return false;
+  if (wk && w.K % 128 != 0) return false;
+  const bool exact = decode_exact() && wk == 0;
+  return encode_tiled() != nullptr && nf4_plan(w.N, w.K, M, r, nf4_esz(w), wk, false, exact, &pl) &&
+         nf4_plan(w.N, w.K, M, r, nf4_esz(w), wk, true, exact, &pl);
 }
 
-template <int DT, int MG, int NT, bool EXACT, bool SS, bool WIN>
+template <int DT, int MG, int NT, bool EXACT, bool SS, bool WIN, int WK>
 static int nf4_launch1(const Nf4Args& q, size_t smem, cudaStream_t st) {
-  auto kern = gemv_nf4_k<DT, MG, NT, EXACT, SS, WIN>;
+  auto kern = gemv_nf4_k<DT, MG, NT, EXACT, SS, WIN, WK>;
   const int rc = ensure_smem_limit((const void*)kern, smem);
   if (rc != RQ_OK) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -1278,15 +1353,27 @@ static int nf4_launch1(const Nf4Args& q, size_t smem, cudaStream_t st) {
   return check_launch();
 }
 
+template <int DT, int MG, int NT, int WK>
+static int nf4_launch_ss(const Nf4Args& q, size_t smem, cudaStream_t st) {
+  if constexpr (nf4_stage_split(MG, NT))
+    if (q.stage_split) return nf4_launch1<DT, MG, NT, false, true, false, WK>(q, smem, st);
+  return nf4_launch1<DT, MG, NT, false, false, false, WK>(q, smem, st);
+}
+
 template <int DT, int MG, int NT, bool EXACT>
 static int nf4_launch(const Nf4Args& q, size_t smem, cudaStream_t st) {
+  // int8 codes (default numerics, no scale windows)
+  if constexpr (!EXACT) {
+    if (q.wk == 1) return nf4_launch_ss<DT, MG, NT, 1>(q, smem, st);
+    if (q.wk == 2) return nf4_launch_ss<DT, MG, NT, 2>(q, smem, st);
+  }
   // scale windows: default numerics, tile split (the plan asks for them
   // only where the whole-pass table leaves a short ring)
   if constexpr (!EXACT)
-    if (q.sw) return nf4_launch1<DT, MG, NT, false, false, true>(q, smem, st);
+    if (q.sw) return nf4_launch1<DT, MG, NT, false, false, true, 0>(q, smem, st);
   if constexpr (nf4_stage_split(MG, NT))
-    if (q.stage_split) return nf4_launch1<DT, MG, NT, EXACT, true, false>(q, smem, st);
-  return nf4_launch1<DT, MG, NT, EXACT, false, false>(q, smem, st);
+    if (q.stage_split) return nf4_launch1<DT, MG, NT, EXACT, true, false, 0>(q, smem, st);
+  return nf4_launch1<DT, MG, NT, EXACT, false, false, 0>(q, smem, st);
 }
 
 template <int DT, int MG, bool EXACT>
@@ -1311,20 +1398,26 @@ static int nf4_dispatch(const Nf4Args& q, const Nf4Plan& pl, cudaStream_t st) {
 int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st) {
   if (g.w.K % 64 || ((uintptr_t)g.w.q % 16) || ((uintptr_t)g.x % 16)) return RQ_ERR_ALIGN;
   Nf4Plan pl;
-  const bool exact = decode_exact();
-  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), beside, exact, &pl)) return RQ_ERR_INVALID;
+  const int wk = nf4_wk(g.w);
+  if (wk && g.w.K % 128) return RQ_ERR_ALIGN;
+  const bool exact = decode_exact() && wk == 0;  // the numerics switch is NF4's
+  if (!nf4_plan(g.w.N, g.w.K, g.M, g.r, nf4_esz(g.w), wk, beside, exact, &pl)) return RQ_ERR_INVALID;
   Nf4Args q;
-  // codes with 128-byte swizzle: 3-D [N][K/256][128] bytes, box 128 x 2 x NT*16
-  // when K % 256 == 0, else 2-D [N][K/2] bytes, box 128 x NT*16;
+  // codes with 128-byte swizzle: NF4 3-D [N][K/256][128] bytes, box 128 x 2 x
+  // NT*16 when K % 256 == 0, else 2-D [N][K/2] bytes, box 128 x NT*16; int8
+  // 3-D [N][K/128][128] bytes, box 128 x 4 x NT*16;
   // X: 32-bit element pairs [M rows][K/2], box 256 x M
   const uint64_t rowb = (uint64_t)(g.w.K / 2), rows = (uint64_t)g.w.N, nt16 = (uint64_t)(pl.nt * 16);
-  q.wide = g.w.K % 256 == 0;
-  int rc = q.wide ? tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 3,
-                                {128, rowb / 128, rows}, {128, rowb}, {128u, 2u, (uint32_t)nt16}},
-                               &q.wmap)
-                  : tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 2,
-                                {rowb, rows, 1}, {rowb, 0}, {128u, (uint32_t)nt16, 1u}},
-                               &q.wmap);
+  q.wide = wk ? 1 : g.w.K % 256 == 0;
+  int rc = wk ? tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 3,
+                            {128, (uint64_t)g.w.K / 128, rows}, {128, (uint64_t)g.w.K}, {128u, 4u, (uint32_t)nt16}},
+                           &q.wmap)
+          : q.wide ? tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 3,
+                                 {128, rowb / 128, rows}, {128, rowb}, {128u, 2u, (uint32_t)nt16}},
+                                &q.wmap)
+                   : tensor_map({g.w.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B, 2,
+                                 {rowb, rows, 1}, {rowb, 0}, {128u, (uint32_t)nt16, 1u}},
+                                &q.wmap);
   if (rc == RQ_OK)
     rc = tensor_map({g.x, CU_TENSOR_MAP_DATA_TYPE_UINT32, CU_TENSOR_MAP_SWIZZLE_NONE, 2,
                      {rowb, (uint64_t)g.M, 1}, {(uint64_t)(g.w.K * 2), 0}, {256u, (uint32_t)g.M, 1u}},
@@ -1339,6 +1432,7 @@ int gemv_nf4_forward(const GemvArgs& g, bool beside, cudaStream_t st) {
   q.esz = pl.esz;
   q.slots = pl.slots;
   q.sw = pl.sw;
+  q.wk = wk;
   q.slot_bytes = pl.slot_bytes;
   q.ring_off = pl.ring_off;
   q.red_off = pl.red_off;
