@@ -1,4 +1,8 @@
-// gemv_kernels.cu -- decode-shaped (M <= 16) fused dequant + GEMV + LoRA.
+// gemv_kernels.cu -- decode-shaped (M <= 16) fused dequant + GEMV + LoRA,
+// register-fed: the int8 formats where their rows cannot travel as the TMA
+// ring's 128-byte pieces (K % 128 != 0, unaligned scales); every other decode
+// call runs on the TMA-ring kernel of gemv_nf4.cu.  Also the dispatch of the
+// decode path (gemv_forward, gemv_supported, gemv_fuse_down).
 //
 // Y[M, N] = X[M, K] . deq(W[N, K])^T, with the LoRA / bias epilogue of
 // LoRALinear.forward.  The weight stream dominates (N*K/2 bytes of NF4 codes

@@ -1,8 +1,13 @@
-// gemv_nf4.cu -- decode-shaped (M <= 16) fused NF4 dequant + GEMV + LoRA.
+// gemv_nf4.cu -- decode-shaped (M <= 16) fused dequant + GEMV + LoRA on a
+// TMA ring.
 //
 // Y[M, N] = X[M, K] . deq(W[N, K])^T with the LoRA / bias epilogue of
 // LoRALinear.forward, for NF4 weights with per-block scales or with
-// double-quantized (fp8 e4m3fnuz or int8) scales.
+// double-quantized (fp8 e4m3fnuz or int8) scales, and for int8 weights with
+// per-block or per-row scales (template WK: a stage row is 512 code bytes,
+// each int8 pair becomes its exact bf16 / f16 pair by two conversions and
+// one packed convert, no table; per-row scales multiply the row sum in the
+// epilogue, as the register-fed int8 kernel of gemv_kernels.cu does).
 //
 // The code stream (N*K/2 bytes) is the cost; the shared-memory data path
 // (128 bytes per clock per SM) is the second limit.  So:
