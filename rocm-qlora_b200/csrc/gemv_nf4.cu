@@ -505,15 +505,28 @@ __device__ __forceinline__ uint32_t ref_pair(uint2 lv, float s) {
   return d;
 }
 
-// int8 codes B and B+1 of `w` as a 16-bit pair (exact: |code| <= 128)
+// int8 codes B and B+1 of a code word as a 16-bit pair (exact: |code| <=
+// 128), from u = word ^ 0x80808080 (each code + 128, as an unsigned byte),
+// without integer-to-float conversions (their pipe is narrow):
+//   bf16: the byte under 0x4B00_0000 is the fp32 2^23 + 128 + v; one packed
+//         fp32 subtraction of 2^23 + 128 leaves v, one packed convert;
+//   f16:  the byte under 0x64 is the half 1024 + 128 + v; one packed half
+//         subtraction of 1152 leaves v.
 template <int DT, int B>
-__device__ __forceinline__ uint32_t i8pair(uint32_t w) {
-  const float f0 = (float)(int8_t)(w >> (8 * B)), f1 = (float)(int8_t)(w >> (8 * B + 8));
+__device__ __forceinline__ uint32_t i8pair(uint32_t u) {
   uint32_t d;
-  if constexpr (DT == RQ_BF16)
+  if constexpr (DT == RQ_BF16) {
+    const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7650u | B), b1 = __byte_perm(u, 0x4B000000u, 0x7650u | (B + 1));
+    unsigned long long t, r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(t) : "r"(b0), "r"(b1));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(t), "l"(0xCB000080CB000080ull));  // - (2^23 + 128), twice
+    float f0, f1;
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(f0), "=f"(f1) : "l"(r));
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f1), "f"(f0));
-  else
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f1), "f"(f0));
+  } else {
+    const uint32_t h = __byte_perm(u, 0x64646464u, (uint32_t)B | (4u << 4) | ((uint32_t)(B + 1) << 8) | (4u << 12));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(h), "r"(0x64806480u));  // - 1152, twice
+  }
   return d;
 }
 
@@ -901,7 +914,9 @@ __global__ void __launch_bounds__(kNfBlockThreads, 1) gemv_nf4_k(const __grid_co
             asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                          : "=r"(h4.x), "=r"(h4.y), "=r"(h4.z), "=r"(h4.w)
                          : "r"(sl + cofs_w + i * kStep * tstep + hstep));
-            const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+            // codes + 128 as unsigned bytes (i8pair)
+            const uint32_t lw[4] = {l4.x ^ 0x80808080u, l4.y ^ 0x80808080u, l4.z ^ 0x80808080u, l4.w ^ 0x80808080u};
+            const uint32_t hw[4] = {h4.x ^ 0x80808080u, h4.y ^ 0x80808080u, h4.z ^ 0x80808080u, h4.w ^ 0x80808080u};
             if constexpr (WK == 2) {
               // per-row scales: the codes multiply straight into the
               // accumulators, the row scale applies in the epilogue
