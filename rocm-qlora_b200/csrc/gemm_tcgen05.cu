@@ -16,19 +16,23 @@
 // dequantized weight is the expensive operand to produce, so each SM
 // dequantizes half of what a one-SM 128 x BN tile would need per FLOP.
 // The reduction step is 64 (one quant block a weight row in the forward;
-// dX steps over 64 weight rows and writes the tile transposed).
+// dX steps over 64 weight rows, whose tile is the MN-major B operand: W's
+// own row layout, so its codes come by TMA like the forward's).
 // 10 warps a CTA:
-//   warp 0   TMA producer of this CTA's activation tile [128 x 64] per
-//            stage (128-byte swizzle) and, once, its LoRA tiles: forward
+//   warp 0   TMA producer of this CTA's activation tile [128 x 64] and
+//            weight codes per stage (128-byte swizzle for the activations)
+//            and, once, its LoRA tiles: forward
 //            t = x.A^T [128 x r] and B [BN/2 x r] (r <= 64, zero-filled to 64
 //            by the TMA bounds); dX gt = rnd(dY*s).B [128 x r] and A [r x BN/2]
-//            (an MN-major operand of 64-column boxes);
+//            (an MN-major operand of 64-column boxes), into the last ring
+//            slot, whose first K-loop fill waits until the LoRA MMAs have
+//            read them;
 //   warp 1   allocates the pair's tensor memory (base accumulator columns
 //            0..BN-1, LoRA accumulator BN..2BN-1, so the epilogue keeps the
 //            reference's rounding sequence).  In the leader CTA (rank 0)
-//            lane 0 issues every MMA of the pair (kind::f16, K = 16, both
-//            operands K-major from shared memory, B of the dX LoRA product
-//            MN-major) and commits each stage to the stage-free barriers of
+//            lane 0 issues every MMA of the pair (kind::f16, K = 16, A
+//            K-major from shared memory, B K-major in the forward and
+//            MN-major in dX) and commits each stage to the stage-free barriers of
 //            BOTH CTAs (tcgen05.commit multicast); in the peer CTA lane 0
 //            signals "both of this CTA's tiles of the stage are ready" to the
 //            leader with a 16-byte bulk copy into the leader's shared memory
@@ -36,14 +40,16 @@
 //            signalling thread, so the signals pipeline);
 //   warps 2-9  dequantize this CTA's half of the weight tile of each stage
 //            as the reference's exact bf16/f16(T[code] * scale) values into
-//            the swizzled K-major layout, arrive on their CTA's fullB, then
+//            the swizzled K-major (dX: MN-major) layout, arrive on their
+//            CTA's fullB, then
 //            run the epilogue on this CTA's 128 rows: tcgen05.ld of both
 //            accumulators, bias and LoRA rounding, Y stores.
 // Barriers: fullA (own TMA bytes), fullB (own 8 dequant warps; in the
 // leader also its producer's expect_tx for the peer's signal), empty (MMA
-// commit), lora / lorafwd (the peer's LoRA-tile signal), acc
-// (final commit, both CTAs).  Grid (2, output tiles, token pairs): the
-// clusters that run together share token rows, so X stays in L2.  Every wait is
+// commit), lora / lorafwd (the peer's LoRA-tile signal), loradone (commit
+// of the LoRA MMAs, both CTAs), acc (final commit, both CTAs).  Grid (2,
+// output tiles, token pairs): the clusters that run together share token
+// rows, so X stays in L2.  Every wait is
 // bounded; a wait that runs out raises the abort flag of both CTAs, each
 // CTA drains what it has in flight (bounded), Y is not written, the pair
 // meets at a cluster barrier before the tensor memory is released, and the
@@ -93,22 +99,27 @@ constexpr uint32_t kLutBytes = 256 * kLutReps * 8;
 constexpr uint32_t kSmemCap = 226 * 1024;   // dynamic shared memory budget (static + margin in the last KB)
 
 // Per-CTA shared-memory plan of a BN-wide pair tile (1 KB aligned offsets);
-// I8: int8 weights (64 code bytes a row and stage instead of 32)
+// I8: int8 weights (64 code bytes a row and stage instead of 32).  The
+// LoRA tiles (t / gt and LoRA B / A) are read only by the LoRA MMAs, which
+// run before the K loop: they lie in the last ring slot (X and weight
+// areas), which the K loop takes over once those MMAs have completed.
 template <int BN, bool I8>
 struct Tile {
   static constexpr int BNH = BN / 2;                  // weight rows (dX: output columns) a CTA
   static constexpr uint32_t kBBytes = BNH * BK * 2;   // 16 KB / 8 KB
-  static constexpr uint32_t kCBytes = BNH * (I8 ? 64 : 32);  // forward: this CTA's code bytes of one stage
+  // this CTA's code bytes of one stage (forward: BNH rows x 32 (64) bytes;
+  // dX: 64 rows x BNH / 2 (BNH) bytes)
+  static constexpr uint32_t kCBytes = BNH * (I8 ? 64 : 32);
   static constexpr uint32_t kStage = kABytes + kBBytes + kCBytes;
-  static constexpr uint32_t kFixed = kABytes + kBBytes + kLutBytes + 1024 + 1024;  // LoRA tiles, LUT, sclut, align
+  static constexpr uint32_t kFixed = kLutBytes + 1024 + 1024;  // LUT, sclut, alignment
   static constexpr int kFit = (int)((kSmemCap - kFixed) / kStage);
   static constexpr int kStages = kFit > 6 ? 6 : kFit;
   static constexpr uint32_t kSmA = 0;                               // kStages x 16 KB
   static constexpr uint32_t kSmB = kSmA + kStages * kABytes;        // kStages x kBBytes
   static constexpr uint32_t kSmC = kSmB + kStages * kBBytes;        // kStages x kCBytes (codes by TMA)
-  static constexpr uint32_t kSmT = kSmC + kStages * kCBytes;        // LoRA t (gt) tile, 16 KB
-  static constexpr uint32_t kSmLB = kSmT + kABytes;                 // LoRA B (dX: A) tile
-  static constexpr uint32_t kSmLut = kSmLB + kBBytes;               // code byte -> (T[lo], T[hi])
+  static constexpr uint32_t kSmT = kSmA + (kStages - 1) * kABytes;  // LoRA t (gt) tile: the last slot's X area
+  static constexpr uint32_t kSmLB = kSmB + (kStages - 1) * kBBytes; // LoRA B (dX: A) tile: its weight area
+  static constexpr uint32_t kSmLut = kSmC + kStages * kCBytes;      // code byte -> (T[lo], T[hi])
   static constexpr uint32_t kSmScl = kSmLut + kLutBytes;            // 256 fp32 second-level values
   static constexpr uint32_t kSmBytes = kSmScl + 1024 + 1024;        // + alignment slack
   static constexpr int kTmemCols = 2 * BN;                          // base + LoRA accumulators
@@ -120,7 +131,8 @@ struct GemmArgs {
   CUtensorMap xmap;   // X [M][K] (dX: dY [M][N]), box 64 x 128, 128-byte swizzle
   CUtensorMap tmap;   // t [M][r] (dX: gt), box 64 x 128, 128-byte swizzle (r < 64 zero-filled)
   CUtensorMap bmap;   // LoRA B [N][r], box 64 x BN/2 (dX: A [r][K], box 64 x 64), 128-byte swizzle
-  CUtensorMap cmap;   // forward: codes uint8 [N][K/2], box 32 x BN/2 (one stage of this CTA's rows)
+  CUtensorMap cmap;   // codes uint8 [N][K/2] (int8 [N][K]): forward box 32 (64) x BN/2 (one stage of this
+                      // CTA's rows), dX box BN/4 (BN/2) x 64 (one stage's rows, this CTA's columns)
   QWeight w;
   const void* bias;
   int bdt;
@@ -311,21 +323,8 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float (&a)
 }
 
 // Read-only global loads pinned where they are written (volatile asm): the
-// dequant warps' prefetch of codes and scales must be issued stages ahead
-// of its use, not sunk to it by the compiler.
-__device__ __forceinline__ uint4 ldg_pin4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-__device__ __forceinline__ uint2 ldg_pin2(const void* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
-}
+// dequant warps' prefetch of scales must be issued stages ahead of its use,
+// not sunk to it by the compiler.
 __device__ __forceinline__ uint32_t ldg_pin_u8(const void* p) {
   uint32_t v;
   asm volatile("ld.global.nc.u8 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -356,8 +355,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
   constexpr int S = TL::kStages, BNH = TL::BNH;
   constexpr uint32_t kBBytes = TL::kBBytes;
   extern __shared__ __align__(1024) unsigned char dsm[];
-  // fullA[S], fullB[S], empty[S], lora, lorafwd, acc, drain
-  __shared__ __align__(8) uint64_t bars[3 * S + 4];
+  // fullA[S], fullB[S], empty[S], lora, lorafwd, acc, drain, loradone
+  __shared__ __align__(8) uint64_t bars[3 * S + 5];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag, a_issued, consumed;
   __shared__ __align__(16) uint32_t sig_src[4], sig_dst[4];  // the 16-byte signal copies (contents unused)
@@ -370,6 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
   unsigned char* sm = dsm + (sbase - sraw);
   const uint32_t fullA0 = smem_u32(bars), fullB0 = fullA0 + 8 * S, empty0 = fullB0 + 8 * S;
   const uint32_t lorabar = empty0 + 8 * S, lorafwd = lorabar + 8, accbar = lorafwd + 8, drainbar = accbar + 8;
+  const uint32_t loradone = drainbar + 8;  // the LoRA MMAs have read the last slot (both CTAs)
   const Abort ab{&abort_flag, mapa(smem_u32(&abort_flag), rank ^ 1u)};
 
   const int M = g.M, N = g.N, K = g.K;
@@ -390,6 +390,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
     mbar_init(lorafwd, 1);
     mbar_init(accbar, 1);
     mbar_init(drainbar, 1);
+    mbar_init(loradone, 1);
     abort_flag = 0;
     a_issued = 0;
     consumed = 0;
@@ -442,17 +443,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       for (int kb = 0; kb < nkb; ++kb) {
         const int slot = kb % S;
         if (kb >= S && !mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab)) break;
+        if (kb == S - 1 && has_lora && !mbar_wait(loradone, 0, ab)) break;  // the LoRA tiles are read
         if (rank == 0) mbar_expect_tx(fullB0 + 8 * slot, 16);  // the peer's "stage ready" signal
-        mbar_expect_tx(fullA0 + 8 * slot, kABytes + (DX ? 0u : TL::kCBytes));
+        mbar_expect_tx(fullA0 + 8 * slot, kABytes + TL::kCBytes);
         tma_2d(sbase + TL::kSmA + slot * kABytes, &g.xmap, kb * BK, m0, fullA0 + 8 * slot);
-        if (!DX) tma_2d(sbase + TL::kSmC + slot * TL::kCBytes, &g.cmap, kb * (I8 ? 64 : 32), nh0, fullA0 + 8 * slot);
+        // the stage's codes: forward this CTA's BNH weight rows of block kb;
+        // dX weight rows 64 kb.. (the reduction), this CTA's BNH columns
+        if (DX)
+          tma_2d(sbase + TL::kSmC + slot * TL::kCBytes, &g.cmap, I8 ? nh0 : nh0 / 2, kb * BK, fullA0 + 8 * slot);
+        else
+          tma_2d(sbase + TL::kSmC + slot * TL::kCBytes, &g.cmap, kb * (I8 ? 64 : 32), nh0, fullA0 + 8 * slot);
         *reinterpret_cast<volatile int*>(&a_issued) = kb + 1;
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ------------------------------------------- MMA issuer (leader CTA)
-      const uint32_t idesc = idesc_pair<DT, BN>();
+      const uint32_t idesc = idesc_pair<DT, BN>(), idesc_mn = idesc_pair<DT, BN>(true);
       bool ok = true;
       if (has_lora) {
         ok = mbar_wait(lorabar, 0, ab) && mbar_wait<true>(lorafwd, 0, ab);
@@ -462,9 +469,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t db = DX ? sw128_mn_desc(sbase + TL::kSmLB + kk * 2048, 8192)  // rows 16kk.. of A
                                    : sw128_desc(sbase + TL::kSmLB + kk * 32);
-            mma_pair(tmem + BN, sw128_desc(sbase + TL::kSmT + kk * 32), db, DX ? idesc_pair<DT, BN>(true) : idesc,
+            mma_pair(tmem + BN, sw128_desc(sbase + TL::kSmT + kk * 32), db, DX ? idesc_mn : idesc,
                      kk > 0);
           }
+          mma_commit_pair(loradone, 3);  // both CTAs' last slot is free once these MMAs have read it
         }
       }
       for (int kb = 0; kb < nkb && ok; ++kb) {
@@ -477,8 +485,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t a = sbase + TL::kSmA + slot * kABytes, b = sbase + TL::kSmB + slot * kBBytes;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          mma_pair(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BK / 16; ++kk)  // dX: the weight tile is MN-major (W's own row layout)
+          mma_pair(tmem, sw128_desc(a + kk * 32), DX ? sw128_mn_desc(b + kk * 2048, 8192) : sw128_desc(b + kk * 32),
+                   DX ? idesc_mn : idesc, (kb > 0 || kk > 0) ? 1u : 0u);
         mma_commit_pair(empty0 + 8 * slot, 3);  // both CTAs' slot is free once these MMAs have read it
         *reinterpret_cast<volatile int*>(&consumed) = kb + 1;
       }
@@ -500,28 +509,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
     }
   } else {
     // ------------------------------------------------ dequant warps (2..9)
-    // Forward: TPR threads share a tile row (weight row nh0 + dt / TPR of
-    // block kb), each converting CW 4-byte code words (NF4: 8 elements, one
-    // 16-byte chunk a word; int8: 4 elements, two words a chunk).  dX: warp
-    // (qb, part) = ((w-2) / 4, (w-2) % 4), lane p: weight rows 64 kb + 2p and
-    // +1, the 16 output columns [16 part, 16 part + 16) of block
-    // nh0 / 64 + qb (NF4: 8 code bytes a row, int8: 16); a warp's 32 lanes
-    // write one shared row's 32 distinct words.  dX codes and scales are
-    // loaded kPrefetch stages ahead.
-    constexpr int CB = I8 ? 64 : 32;      // code bytes of a row and stage
-    constexpr int TPR = 256 / BNH;        // forward: threads a row (2 or 4)
-    constexpr int CW = (CB / 4) / TPR;    // forward: code words a thread
-    constexpr int QB = BNH / 64;    // dX: quant blocks of a weight row a CTA covers (2 or 1)
+    // Both directions take the stage's codes from its TMA copy and store
+    // 16-byte units (8 elements) of 128-byte rows, unit c of row n at
+    // (c ^ (n & 7)).  Forward: the K-major tile, TPR threads a tile row
+    // (weight row nh0 + frow, the 64 elements of block kb).  dX: the
+    // MN-major tile, which is W's own row layout: weight row 64 kb + frow
+    // (the reduction index), this CTA's BNH output columns in 64-column
+    // chunks of 8 KB; 4 threads a row, BNH / 4 columns each (half or a
+    // quarter of one quant block).  For BNH = 128 a quarter warp (the lanes
+    // one 16-byte store phase serves) takes 4 rows x 2 column quarters of
+    // one chunk, so its 8 stores hit 8 distinct bank groups.
+    constexpr int CB = I8 ? 64 : 32;                                    // forward: code bytes of a row and stage
+    constexpr int TPR = DX ? 4 : 256 / BNH;                             // threads a row
+    constexpr int CW = DX ? (I8 ? BNH / 16 : BNH / 32) : (CB / 4) / TPR;  // code words a thread
+    constexpr int RB = DX ? (I8 ? BNH : BNH / 2) : CB;                  // code bytes of a row in the stage
+    constexpr int UPT = I8 ? CW / 2 : CW;                               // 16-byte units a thread stores
     const int dt = tid - 64;
     const int fmt = g.w.fmt;
     // first-level scales per block (NF4 / int8) or per row (int8 per-row);
     // otherwise double-quantized (c2 code x c2_scales)
     const bool plain = fmt == RQ_W_NF4 || fmt == RQ_W_INT8, rowsc = fmt == RQ_W_INT8_ROW;
     const int nbk = K / 64;
-    const uint8_t* qb = static_cast<const uint8_t*>(g.w.q);
-    const int frow = dt / TPR, fpart = dt % TPR;
-    const int dq = (warp - 2) >> 2, dpart = (warp - 2) & 3, p = lane;
-    const bool dx_active = dq < QB;
+    int frow, fpart;
+    if constexpr (DX && BNH == 128) {
+      const int q = lane >> 3, idx = lane & 7;
+      frow = 8 * (warp - 2) + 4 * (q >> 1) + (idx & 3);
+      fpart = (idx >> 2) + 2 * (q & 1);
+    } else {
+      frow = dt / TPR;
+      fpart = dt % TPR;
+    }
+    const int dcol = DX ? fpart * (BNH / 4) : 0;  // dX: first of the thread's output columns in the CTA's half
+    const uint32_t row_off = (uint32_t)(dcol / 64) * 8192u + (uint32_t)frow * 128u;
+    const int ub = DX ? (dcol % 64) / 8 : fpart * UPT;  // the thread's first unit in its row
     const uint32_t lut_lane = smem_u32(lutp) + (uint32_t)(lane & (kLutReps - 1)) * 8;
     // (T[lo], T[hi]) of byte J of `w`: one byte permute, one multiply-add, one 8-byte load
     auto lut_at = [&](uint32_t w, int j) -> float2 {
@@ -530,148 +550,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
       return v;
     };
-    struct Raw {
-      uint32_t c[8];  // dX: the code words of the two rows (NF4: 2 each, int8: 4 each)
-      uint32_t c2b[2];
-      float sraw[2];
-    };
-    auto fetch = [&](int kb, Raw& r) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) r.c[i] = 0u;
-      r.c2b[0] = r.c2b[1] = 0u;
-      r.sraw[0] = r.sraw[1] = 0.0f;
-      if (kb >= nkb) return;
-#pragma unroll
-      for (int h = 0; h < (DX ? 2 : 1); ++h) {
-        const int n = DX ? kb * 64 + 2 * p + h : nh0 + frow;
-        const int blk = DX ? (nh0 >> 6) + dq : kb;
-        if (DX ? (dx_active && blk < nbk) : n < N) {
-          const uint8_t* src = qb + (size_t)n * (size_t)(I8 ? K : K / 2) + (size_t)blk * CB;
-          if (DX && I8) {  // forward codes arrive by TMA with the stage
-            const uint4 v = ldg_pin4(reinterpret_cast<const uint4*>(src) + dpart);
-            r.c[4 * h] = v.x;
-            r.c[4 * h + 1] = v.y;
-            r.c[4 * h + 2] = v.z;
-            r.c[4 * h + 3] = v.w;
-          } else if (DX) {
-            const uint2 v = ldg_pin2(reinterpret_cast<const uint2*>(src) + dpart);
-            r.c[2 * h] = v.x;
-            r.c[2 * h + 1] = v.y;
-          }
-          const int64_t bi = (int64_t)n * nbk + blk;
-          if (plain || rowsc) {
-            r.sraw[h] = load_scalar(g.w.scales, g.w.sdt, rowsc ? (int64_t)n : bi);
-          } else {
-            r.c2b[h] = ldg_pin_u8(g.w.c2 + bi);
-            r.sraw[h] = ldg_pin_f32(g.w.c2s + bi / kDQBlock2);
-          }
-        }
-      }
-    };
-    // sv0 / sv1: the block scales of the stage (forward: sv0 of this row;
-    // dX: of weight rows 64 kb + 2p and +1); r: dX codes
-    auto convert = [&](int kb, const Raw& r, float sv0, float sv1) -> bool {
+    // sv: the block scale of the thread's elements in stage kb
+    auto convert = [&](int kb, float sv) -> bool {
       const int slot = kb % S;
-      const float sv[2] = {sv0, sv1};
       // lane 0 polls the barrier (the other lanes wait in the shuffle, so
       // the shared-memory pipe the TMA writes through is not flooded with
-      // polls), and the warp takes one decision
-      // forward: the stage's TMA (X and this CTA's codes) has landed, which
-      // also means the slot's previous MMAs are done (the producer issued it
-      // only after they were); dX: the slot is free
+      // polls), and the warp takes one decision: the stage's TMA (X or dY
+      // and this CTA's codes) has landed, which also means the slot's
+      // previous MMAs are done (the producer issued it only after they were)
       bool free_slot = true;
-      if (!DX && lane == 0)
-        free_slot = mbar_wait(fullA0 + 8 * slot, (kb / S) & 1, ab);
-      else if (DX && kb >= S && lane == 0)
-        free_slot = mbar_wait(empty0 + 8 * slot, ((kb / S) - 1) & 1, ab);
+      if (lane == 0) free_slot = mbar_wait(fullA0 + 8 * slot, (kb / S) & 1, ab);
       if (!__shfl_sync(0xffffffffu, (int)free_slot, 0)) return false;
-      unsigned char* bt = sm + TL::kSmB + slot * kBBytes;
-      if (DX && I8) {
-        if (dx_active) {
-          // tile row kr (= output column), 16-bit pair (n, n+1) at word p;
-          // byte j of word i is output column 4 i + j of the thread's 16
-          const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float f0 = (float)(int8_t)(r.c[i] >> (8 * j)), f1 = (float)(int8_t)(r.c[4 + i] >> (8 * j));
-              const int kr = dq * 64 + dpart * 16 + i * 4 + j;
-              unsigned char* r0 = bt + (kr >> 3) * 1024 + (kr & 7) * 128 + colo;
-              *reinterpret_cast<uint32_t*>(r0 + ((colb ^ (kr & 7)) << 4)) = pack_rn<DT>(f0 * sv[0], f1 * sv[1]);
-            }
+      unsigned char* rowp = sm + TL::kSmB + slot * kBBytes + row_off;
+      uint32_t cw[CW];  // this thread's code words of the stage (TMA-landed)
+      {
+        const unsigned char* cs = sm + TL::kSmC + slot * TL::kCBytes + frow * RB + fpart * (CW * 4);
+        if constexpr (CW == 8) {
+          const uint4 v = *reinterpret_cast<const uint4*>(cs), v2 = *reinterpret_cast<const uint4*>(cs + 16);
+          cw[0] = v.x;
+          cw[1] = v.y;
+          cw[2] = v.z;
+          cw[3] = v.w;
+          cw[4] = v2.x;
+          cw[5] = v2.y;
+          cw[6] = v2.z;
+          cw[7] = v2.w;
+        } else if constexpr (CW == 4) {
+          const uint4 v = *reinterpret_cast<const uint4*>(cs);
+          cw[0] = v.x;
+          cw[1] = v.y;
+          cw[2] = v.z;
+          cw[3] = v.w;
+        } else {
+          const uint2 v = *reinterpret_cast<const uint2*>(cs);
+          cw[0] = v.x;
+          cw[1] = v.y;
         }
-      } else if (DX) {
-        if (dx_active) {
-          // tile row kr (= output column), 16-bit pair (n, n+1) at word p
-          const uint32_t colb = (uint32_t)(p >> 2), colo = (uint32_t)(p & 3) * 4;
+      }
+      if constexpr (I8) {
+        // int8: bf16/f16(float(q) * scale), two words a unit
 #pragma unroll
-          for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < UPT; ++i) {
+          uint32_t qv[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 l0 = lut_at(r.c[i], j), l1 = lut_at(r.c[2 + i], j);
-              const int kr = dq * 64 + dpart * 16 + i * 8 + j * 2;  // tile rows kr (low nibbles), kr + 1 (high)
-              unsigned char* r0 = bt + (kr >> 3) * 1024 + (kr & 7) * 128 + colo;
-              unsigned char* r1 = bt + ((kr + 1) >> 3) * 1024 + ((kr + 1) & 7) * 128 + colo;
-              *reinterpret_cast<uint32_t*>(r0 + ((colb ^ (kr & 7)) << 4)) = pack_rn<DT>(l0.x * sv[0], l1.x * sv[1]);
-              *reinterpret_cast<uint32_t*>(r1 + ((colb ^ ((kr + 1) & 7)) << 4)) =
-                  pack_rn<DT>(l0.y * sv[0], l1.y * sv[1]);
-            }
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t w = cw[2 * i + (j >> 1)];
+            const int b = (j & 1) * 16;
+            qv[j] = pack_rn<DT>((float)(int8_t)(w >> b) * sv, (float)(int8_t)(w >> (b + 8)) * sv);
+          }
+          *reinterpret_cast<uint4*>(rowp + (((ub + i) ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
         }
       } else {
-        // 8 chunks of 16 bytes (8 elements) a row; chunk c at (c ^ (row & 7))
-        unsigned char* rowp = bt + (frow >> 3) * 1024 + (frow & 7) * 128;
-        uint32_t cw[CW];  // this thread's code words of the stage (TMA-landed)
-        {
-          const unsigned char* cs = sm + TL::kSmC + slot * TL::kCBytes + frow * CB + fpart * (CW * 4);
-          if constexpr (CW == 8) {
-            const uint4 v = *reinterpret_cast<const uint4*>(cs), v2 = *reinterpret_cast<const uint4*>(cs + 16);
-            cw[0] = v.x;
-            cw[1] = v.y;
-            cw[2] = v.z;
-            cw[3] = v.w;
-            cw[4] = v2.x;
-            cw[5] = v2.y;
-            cw[6] = v2.z;
-            cw[7] = v2.w;
-          } else if constexpr (CW == 4) {
-            const uint4 v = *reinterpret_cast<const uint4*>(cs);
-            cw[0] = v.x;
-            cw[1] = v.y;
-            cw[2] = v.z;
-            cw[3] = v.w;
-          } else {
-            const uint2 v = *reinterpret_cast<const uint2*>(cs);
-            cw[0] = v.x;
-            cw[1] = v.y;
+#pragma unroll
+        for (int i = 0; i < UPT; ++i) {
+          uint32_t qv[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 l = lut_at(cw[i], j);
+            qv[j] = pack_rn<DT>(l.x * sv, l.y * sv);
           }
-        }
-        if constexpr (I8) {
-          // int8: bf16/f16(float(q) * scale), two words a chunk
-#pragma unroll
-          for (int i = 0; i < CW / 2; ++i) {
-            const int c = fpart * (CW / 2) + i;
-            uint32_t qv[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t w = cw[2 * i + (j >> 1)];
-              const int b = (j & 1) * 16;
-              qv[j] = pack_rn<DT>((float)(int8_t)(w >> b) * sv[0], (float)(int8_t)(w >> (b + 8)) * sv[0]);
-            }
-            *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < CW; ++i) {
-            const int c = fpart * CW + i;
-            uint32_t qv[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 l = lut_at(cw[i], j);
-              qv[j] = pack_rn<DT>(l.x * sv[0], l.y * sv[0]);
-            }
-            *reinterpret_cast<uint4*>(rowp + ((c ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
-          }
+          *reinterpret_cast<uint4*>(rowp + (((ub + i) ^ (frow & 7)) << 4)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
@@ -680,21 +618,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       return true;
     };
     if constexpr (DX) {
-      // a register ring of kPrefetch stages of codes and scales (static
+      // dX: the thread's block scale changes with the weight row, 64 rows a
+      // stage; a register ring holds kPrefetch stages of raw scales (static
       // indices: fully unrolled)
-      Raw ring[kPrefetch];
+      const int blk = (nh0 + dcol) / 64;
+      struct DSc {
+        uint32_t v;  // plain scale (fp32 bits) or c2 byte
+        float s2;    // c2_scale
+      };
+      auto dfetch = [&](int kb, DSc& q) {
+        q.v = 0u;
+        q.s2 = 0.0f;
+        if (kb >= nkb || blk >= nbk) return;
+        const int64_t n = (int64_t)kb * 64 + frow, bi = n * nbk + blk;
+        if (plain || rowsc) {
+          q.v = __float_as_uint(load_scalar(g.w.scales, g.w.sdt, rowsc ? n : bi));
+        } else {
+          q.v = ldg_pin_u8(g.w.c2 + bi);
+          q.s2 = ldg_pin_f32(g.w.c2s + bi / kDQBlock2);
+        }
+      };
+      DSc ring[kPrefetch];
 #pragma unroll
-      for (int i = 0; i < kPrefetch; ++i) fetch(i, ring[i]);
+      for (int i = 0; i < kPrefetch; ++i) dfetch(i, ring[i]);
       bool go = true;
       for (int kb = 0; kb < nkb && go; kb += kPrefetch) {
 #pragma unroll
         for (int i = 0; i < kPrefetch; ++i) {
           if (go && kb + i < nkb) {
-            const Raw& r = ring[i];
-            const float s0 = (plain || rowsc) ? r.sraw[0] : sclut[r.c2b[0]] * r.sraw[0];
-            const float s1 = (plain || rowsc) ? r.sraw[1] : sclut[r.c2b[1]] * r.sraw[1];
-            go = convert(kb + i, r, s0, s1);
-            fetch(kb + i + kPrefetch, ring[i]);
+            const float sv = (plain || rowsc) ? __uint_as_float(ring[i].v) : sclut[ring[i].v & 255u] * ring[i].s2;
+            go = convert(kb + i, sv);
+            dfetch(kb + i + kPrefetch, ring[i]);
           }
         }
       }
@@ -730,7 +684,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
       };
       Group gr;  // the next group's raw scales, in flight while 16 stages run
       group_fetch(0, gr);
-      const Raw none{};
       bool go = true;
       for (int g0 = 0; g0 < nkb && go; g0 += 16) {
         float sg[16];
@@ -742,7 +695,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) gemm_k(
                                         (((b0 + j) / kDQBlock2) != (b0 / kDQBlock2) ? gr.s2[1] : gr.s2[0]);
         group_fetch(g0 / 16 + 1, gr);
 #pragma unroll 1
-        for (int j = 0; j < 16 && go && g0 + j < nkb; ++j) go = convert(g0 + j, none, sg[j], 0.0f);
+        for (int j = 0; j < 16 && go && g0 + j < nkb; ++j) go = convert(g0 + j, sg[j]);
       }
     }
 
@@ -1104,15 +1057,15 @@ static int gemm_launch(const LinearArgs& a, bool dx, const void* a_op, const voi
     g.bmap = g.xmap;
   }
   const bool i8 = !is_nf4_fmt(a.w.fmt);
-  if (!dx) {  // codes [N][K/2] (int8: [N][K]) bytes, a CTA's bn/2 rows x 32 (64) bytes a stage
+  {  // codes [N][K/2] (int8: [N][K]) bytes; a stage's box: forward a CTA's
+     // bn/2 rows x 32 (64) bytes, dX 64 rows x the bytes of a CTA's bn/2 columns
     const uint64_t rowb = i8 ? K : K / 2;
     const uint64_t d[3] = {rowb, N, 1}, sd[2] = {rowb, 0};
-    const uint32_t b[3] = {i8 ? 64u : 32u, (uint32_t)(bn / 2), 1};
+    const uint32_t half = (uint32_t)(bn / 2);
+    const uint32_t b[3] = {dx ? (i8 ? half : half / 2) : (i8 ? 64u : 32u), dx ? 64u : half, 1};
     const int rc = tensor_map_encode(CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_NONE, 2, a.w.q, d, sd, b,
                                      &g.cmap);
     if (rc != RQ_OK) return rc;
-  } else {
-    g.cmap = g.xmap;
   }
   g.w = a.w;
   g.bias = dx ? nullptr : a.bias;
