@@ -91,9 +91,9 @@ constexpr int BK = 64;
 constexpr int kDqWarps = 8;                 // dequant / epilogue warps
 constexpr int kThreads = 64 + kDqWarps * 32;
 constexpr uint32_t kABytes = BM * BK * 2;   // 16 KB
-constexpr uint32_t kWaitLimit = 1u << 22;   // polls of a bounded wait (each at least kPollNs apart)
+constexpr uint32_t kWaitLimit = 1u << 22;   // polls of a bounded drain (each at least kPollNs apart)
 constexpr uint32_t kPollNs = 32;
-constexpr int kPrefetch = 4;                // stages of codes and scales a dequant thread holds in registers
+constexpr int kPrefetch = 4;                // dX: stages of block scales a dequant thread holds in registers
 constexpr int kLutReps = 16;                // copies of the code-byte table (one per half-warp lane)
 constexpr uint32_t kLutBytes = 256 * kLutReps * 8;
 constexpr uint32_t kSmemCap = 226 * 1024;   // dynamic shared memory budget (static + margin in the last KB)
@@ -213,17 +213,49 @@ struct Abort {
   }
 };
 
+// Potentially blocking test of a phase (try_wait: a thread whose phase is
+// not complete is suspended in the barrier until it completes or a
+// system-dependent time limit passes, so it neither polls the barrier word
+// nor oversleeps the completion).
+template <bool kCluster>
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  if constexpr (kCluster)
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+  else
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t gtimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr uint64_t kWaitNs = 2000000000ull;  // a bounded wait gives up after about 2 s
+
 // Bounded wait for the phase of parity `parity`; false if either CTA of the
 // pair gave up (then or earlier).
 template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_test<kCluster>(bar, parity)) return true;
-    if (ab.raised()) return false;
-    __nanosleep(kPollNs);  // a paced poll: the barrier word is not hammered
+  if (mbar_try<kCluster>(bar, parity)) return true;
+  const uint64_t t0 = gtimer_ns();
+  while (!ab.raised()) {
+    if (mbar_try<kCluster>(bar, parity)) return true;
+    if (gtimer_ns() - t0 > kWaitNs) {
+      ab.raise();
+      atomicAdd(&g_gemm_timeouts, 1u);
+      return false;
+    }
   }
-  ab.raise();
-  atomicAdd(&g_gemm_timeouts, 1u);
   return false;
 }
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
