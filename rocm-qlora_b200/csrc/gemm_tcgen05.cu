@@ -1151,7 +1151,10 @@ int lora_down_tc(int dt, bool wt, const void* X, int64_t M, int64_t Kr, const vo
     if (rc != RQ_OK) return rc;
   }
   const int64_t tiles = (M + 127) / 128, nsteps = Kr / 64;
-  int64_t sk = (2 * (int64_t)num_sms() + tiles - 1) / tiles;
+  // split-K depth: the deepest that keeps the grid in one round (two CTAs
+  // fit an SM); one more (the rounded-up share) left a second round of a
+  // few clusters that doubled the call (M = 8192: 320 CTAs for 296 slots)
+  int64_t sk = 2 * (int64_t)num_sms() / tiles;
   if (sk > 8) sk = 8;
   if (sk > nsteps) sk = nsteps;
   if (sk < 1) sk = 1;
