@@ -1,4 +1,6 @@
-"""HuggingFace integration (config only in this build)."""
+"""HuggingFace integration: the quantization config and the HfQuantizer
+(the reference's rocm_qlora/hf_integration/__init__.py exports)."""
 from rocm_qlora.hf_integration.config import RocmQLoraConfig
+from rocm_qlora.hf_integration.quantizer import RocmQLoraQuantizer
 
-__all__ = ["RocmQLoraConfig"]
+__all__ = ["RocmQLoraConfig", "RocmQLoraQuantizer"]
