@@ -328,9 +328,13 @@ def run_ours(args, rank, world, device):
     e2e = run_e2e(args, rotated_modules(layers, wsets), device, world)
 
     # CPU baseline on rank 0 (bounded sample of the same workload)
-    cpu = cpu_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
-    # configs[2] (prefill / training GEMM), single GPU
+    cpu_layers = _cpu_layers() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    cpu = cpu_baseline(args, cpu_layers) if cpu_layers is not None else None
+    # configs[2] (prefill / training GEMM), single GPU, with the reference's
+    # CPU path timed beside it
     prefill = prefill_leg(device) if (world == 1 and not args.no_prefill) else None
+    if prefill is not None and cpu_layers is not None:
+        prefill["cpu_baseline"] = prefill_cpu_baseline(cpu_layers)
     c5 = c5_leg(device) if (world == 1 and not args.no_prefill) else None
     if world > 1 and not args.no_prefill:
         c5 = c5_sharded_leg(device, rank, world)
@@ -950,6 +954,34 @@ def cpu_baseline(args, layers=None, seconds=12.0):
             "kind": "port",
             "sample": f"{n} LoRALinear forwards of the sweep (torch CPU eager ops of the reference, "
                       f"{t_total:.1f} s)"}
+
+
+def prefill_cpu_baseline(layers, seconds=6.0):
+    """The reference's eager CPU path for the prefill metric (torch ops
+    restated in oracle/torch_port.py), timed on this host with all its
+    threads on a bounded sample of configs[2]: forward calls of the
+    4096x4096 NF4 + double-quant layer at M = 512 with an r = 64 adapter
+    (the smallest of the leg's calls), TFLOP/s counted as in prefill_leg."""
+    from oracle import torch_port
+    from tests.inputs import layer_inputs
+    torch.set_num_threads(os.cpu_count() or 1)
+    N, K, packed, c2, c2s, _, _ = layers[0]
+    inp = layer_inputs(N, K, 1, sigma=0.02, r=PREFILL_R, alpha=PREFILL_ALPHA, seed=200)
+    M = PREFILL_MS[0]
+    fl = 2.0 * M * N * K + 2.0 * M * PREFILL_R * (K + N)
+    g = torch.Generator().manual_seed(5)
+    n, t_total = 0, 0.0
+    while t_total < seconds or n == 0:
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            torch_port.loralinear_forward_dq(x, packed, c2, c2s, N, K, inp.A, inp.B, PREFILL_ALPHA / PREFILL_R)
+        t_total += time.perf_counter() - t0
+        n += 1
+    return {"value": round(fl * n / t_total / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} LoRALinear forwards of the {N}x{K} layer at M={M}, r={PREFILL_R} "
+                      f"(torch CPU eager ops of the reference, {t_total:.1f} s)"}
 
 
 def run_reference(args, rank, world):
